@@ -1,0 +1,116 @@
+"""Philox4x32-10 counter-based generator, restated in numpy (oracle; test infrastructure only).
+
+The algorithm is the published Philox4x32 of Salmon, Moraes, Dror and Shaw,
+"Parallel random numbers: as easy as 1, 2, 3" (SC'11): ten rounds of two
+32x32->64 multiplies by 0xD2511F53 / 0xCD9E8D57, with the key bumped by the
+Weyl constants 0x9E3779B9 / 0xBB67AE85 after every round.  Triton's
+``tl.rand`` (triton 3.6.0, ``triton/language/random.py``) is this generator with
+counter ``(offset, 0, 0, 0)`` and key ``(seed_lo, seed_hi)``; the reference's
+optimizer kernels draw from it (``ecoint8/triton_kernels.py:87,113,116``).
+
+``sr_word`` / ``sr_nudge`` define the stochastic-rounding stream of the CUDA
+library (its Philox mode); the CUDA device code implements the same function.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+M0 = np.uint64(0xD2511F53)
+M1 = np.uint64(0xCD9E8D57)
+W0 = 0x9E3779B9
+W1 = 0xBB67AE85
+MASK32 = np.uint64(0xFFFFFFFF)
+
+
+def philox4x32(c0, c1, c2, c3, k0: int, k1: int, rounds: int = 10):
+    """Vectorised Philox4x32-R.  Counters are arrays of uint32 values; key is two ints."""
+    c0 = np.asarray(c0, dtype=np.uint64) & MASK32
+    c1 = np.asarray(c1, dtype=np.uint64) & MASK32
+    c2 = np.asarray(c2, dtype=np.uint64) & MASK32
+    c3 = np.asarray(c3, dtype=np.uint64) & MASK32
+    c0, c1, c2, c3 = np.broadcast_arrays(c0, c1, c2, c3)
+    k0 &= 0xFFFFFFFF
+    k1 &= 0xFFFFFFFF
+    for _ in range(rounds):
+        p0 = M0 * c0  # < 2**64, exact in uint64
+        p1 = M1 * c2
+        n0 = (p1 >> np.uint64(32)) ^ c1 ^ np.uint64(k0)
+        n2 = (p0 >> np.uint64(32)) ^ c3 ^ np.uint64(k1)
+        c1 = p1 & MASK32
+        c3 = p0 & MASK32
+        c0, c2 = n0, n2
+        k0 = (k0 + W0) & 0xFFFFFFFF
+        k1 = (k1 + W1) & 0xFFFFFFFF
+    return c0, c1, c2, c3
+
+
+def sr_word(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
+    """64 random bits for element ``(row, col)`` of stochastic-rounding site ``stream``.
+
+    Counter ``(col >> 1, row, stream_lo, stream_hi)``, key ``(seed_lo, seed_hi)``;
+    an even column takes words ``(x1:x0)``, an odd column ``(x3:x2)``.
+    Returns uint64.
+    """
+    rows = np.asarray(rows, dtype=np.uint64)
+    cols = np.asarray(cols, dtype=np.uint64)
+    rows, cols = np.broadcast_arrays(rows, cols)
+    x0, x1, x2, x3 = philox4x32(cols >> np.uint64(1), rows, stream & 0xFFFFFFFF,
+                                (stream >> 32) & 0xFFFFFFFF, seed & 0xFFFFFFFF,
+                                (seed >> 32) & 0xFFFFFFFF)
+    lo = np.where((cols & np.uint64(1)) == 0, x0, x2)
+    hi = np.where((cols & np.uint64(1)) == 0, x1, x3)
+    return (hi << np.uint64(32)) | lo
+
+
+def low_bits(word: np.ndarray, nbits: int) -> np.ndarray:
+    """``word mod 2**nbits`` as int64 (0 <= nbits <= 63)."""
+    if nbits <= 0:
+        return np.zeros(word.shape, dtype=np.int64)
+    return (word & np.uint64((1 << nbits) - 1)).astype(np.int64)
+
+
+def sr_nudge(seed: int, stream: int, shape, shift: int, row_base: int = 0) -> np.ndarray:
+    """``U[0, 2**shift)`` nudges for a ``[rows, cols]`` site (row index offset by ``row_base``)."""
+    rows, cols = (shape if len(shape) == 2 else (int(np.prod(shape[:-1])), shape[-1]))
+    r = np.arange(rows, dtype=np.uint64)[:, None] + np.uint64(row_base)
+    c = np.arange(cols, dtype=np.uint64)[None, :]
+    return low_bits(sr_word(seed, stream, r, c), shift).reshape(shape)
+
+
+STEP_M_SPLIT = 52  # momentum nudges up to 52 bits share the weight nudge's word
+STREAM_ALT = 1 << 63
+
+
+def step_nudges(seed: int, stream: int, rows: int, cols: int, com_mm: int):
+    """Weight (12-bit) and momentum (``com_mm``-bit) nudges of one I8ECO layer step.
+
+    Both come from one 64-bit word per element: the weight nudge is its low 12
+    bits, the momentum nudge the next ``com_mm`` bits when ``com_mm <= 52``;
+    otherwise the momentum nudge is the low ``com_mm`` bits of the word of
+    stream ``stream | 2**63``.
+    """
+    r = np.arange(rows, dtype=np.uint64)[:, None]
+    c = np.arange(cols, dtype=np.uint64)[None, :]
+    word = sr_word(seed, stream, r, c)
+    nw = low_bits(word, 12)
+    if com_mm < 0:
+        nm = None
+    elif com_mm <= STEP_M_SPLIT:
+        nm = low_bits(word >> np.uint64(12), com_mm)
+    else:
+        nm = low_bits(sr_word(seed, stream | STREAM_ALT, r, c), com_mm)
+    return nw, nm
+
+
+def tl_rand(seed: int, offsets: np.ndarray) -> np.ndarray:
+    """``tl.rand(seed, offsets)`` for int32 offsets: uniform fp32 in [0, 1).
+
+    Counter ``(offset, 0, 0, 0)``; the first output word, viewed as int32 and
+    folded (``x < 0 -> -x - 1``), times fp32 4.6566127342e-10.
+    """
+    off = np.asarray(offsets, dtype=np.int64).astype(np.uint64) & MASK32
+    x0, _, _, _ = philox4x32(off, 0, 0, 0, seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)
+    xi = x0.astype(np.uint32).view(np.int32).astype(np.int64)
+    xi = np.where(xi < 0, -xi - 1, xi).astype(np.int32)
+    return (xi.astype(np.float32) * np.float32(4.6566127342e-10)).astype(np.float32)
