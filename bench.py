@@ -1,0 +1,459 @@
+"""Benchmark of the strict int8 ECO training step on B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1: one rank per GPU)
+
+Headline (``value``): training steps/s of the deep strict-int8 MLP -- 8
+``I8Linear(8192, 8192)`` + ``I8ReLU`` blocks and ``I8Linear(8192, 1000)`` --
+at a global batch of 16384 Gaussian samples with random labels, I8ECO
+(momentum 0.9).  One step = forward_i8 + the fp32 loss boundary (cross
+entropy, stochastic gradient quantization) + backward_i8 + I8ECO.step.  With N
+GPUs the global batch is split across ranks (strong scaling; int32 dW summed
+over NCCL).  Inputs are larger than L2 (no flush needed).
+
+Also measured on rank 0 at N=1: the fused forward GEMM (TOPS, the roofline
+kernel), the int32 GEMM, and the standalone I8ECO step over 64 layers of
+4096x4096 (HBM GB/s); and the oracle port of the reference on the host cores
+(``cpu_baseline``).  ``--impl reference`` times only that CPU port.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "eco-int8-opt_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+LAYERS = [(8192, 8192)] * 8 + [(8192, 1000)]
+GLOBAL_BATCH = 16384
+METRIC = "int8 train steps/s (deep MLP 8x8192^2+8192->1000, global batch 16384)"
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- launch counter
+KERNELS_PER_CALL = {"eco_gemm_s8s32": 1, "eco_gemm_s8_requant": 1, "eco_requant_s32_s8": 1,
+                    "eco_apply_mult_shift": 1, "eco_colsum_s8": 1, "eco_amax": 2, "eco_sumsq_s8": 1,
+                    "eco_i8eco_step": 1, "eco_sgdm_step": 3}
+
+
+class LaunchCounter:
+    def __init__(self):
+        from ecoint8 import _native
+
+        self.nat = _native
+        self.count = 0
+        self.orig = _native.call
+
+    def __enter__(self):
+        def counting(name, *args):
+            self.count += KERNELS_PER_CALL.get(name, 0)
+            return self.orig(name, *args)
+
+        self.nat.call = counting
+        # the modules bound `call` through the module, so patching the attribute is enough
+        return self
+
+    def __exit__(self, *exc):
+        self.nat.call = self.orig
+
+
+# ----------------------------------------------------------------------------- model
+def fast_layer(in_f, out_f, gen, device):
+    """I8Linear with the reference's init formula (ilayer.py:96-101) evaluated on the GPU."""
+    from ecoint8 import I8Linear
+
+    lin = I8Linear(1, 1)
+    w_fp = torch.randn(out_f, in_f, generator=gen, device=device) * (2.0 / in_f) ** 0.5
+    amax = w_fp.abs().amax(dim=1)
+    sw = (amax / 127.0 * lin.headroom).clamp_min(1e-8)
+    lin.w_i8 = torch.clamp(torch.round(w_fp / sw.unsqueeze(1)), -127, 127).to(torch.int8)
+    lin.sw = [float(v) for v in sw.cpu()]
+    lin.b_acc = torch.zeros(out_f, dtype=torch.int32, device=device)
+    return lin
+
+
+def build_mlp(device, seed=0):
+    from ecoint8 import I8ReLU, I8Sequential
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    blocks = []
+    for i, (a, b) in enumerate(LAYERS):
+        blocks.append(fast_layer(a, b, gen, device))
+        if i + 1 < len(LAYERS):
+            blocks.append(I8ReLU())
+    return I8Sequential(*blocks).to(device)
+
+
+def loss_boundary(logits_i8, s_out, y, global_batch, world):
+    """fp32 boundary of examples/i8_demo.py:56-61: CE over the global batch, SR quantization of the grad."""
+    import torch.distributed as dist
+
+    from ecoint8.quant import calc_scale, quantize_symmetric
+
+    logits = (logits_i8.to(torch.float32) * s_out).requires_grad_()
+    loss = torch.nn.functional.cross_entropy(logits, y, reduction="sum") / global_batch
+    (g,) = torch.autograd.grad(loss, logits)
+    amax = g.detach().abs().max()
+    if world > 1:
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(loss, op=dist.ReduceOp.SUM)
+    s_g = calc_scale(amax.item())
+    return loss.detach(), quantize_symmetric(g, s_g, stochastic=True), s_g
+
+
+def train_step(net, opt, x_i8, y, world):
+    logits, s_out = net.forward_i8(x_i8)
+    loss, g_i8, s_g = loss_boundary(logits, s_out, y, GLOBAL_BATCH, world)
+    net.backward_i8(g_i8, s_g)
+    opt.step()
+    opt.zero_grad()
+    return loss
+
+
+# ----------------------------------------------------------------------------- side measurements
+def time_kernel(fn, iters=10, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters / 1e3  # s per launch
+
+
+def gemm_measurements(device):
+    from ecoint8 import _native, _ops, _sr
+
+    M, N, K = 16384, 8192, 8192
+    gen = torch.Generator(device=device).manual_seed(1)
+    x = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=device, generator=gen)
+    w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=device, generator=gen)
+    bias = torch.randint(-1000, 1000, (N,), dtype=torch.int32, device=device, generator=gen)
+    mult = torch.randint(1 << 20, 1 << 21, (N,), dtype=torch.int32, device=device, generator=gen)
+    site = _sr.Site(_native.sr_spec(_native.SR_PHILOX, seed=7, stream_id=0), None)
+    y = torch.empty((M, N), dtype=torch.int8, device=device)
+    t_fused = time_kernel(lambda: _ops.gemm_requant(x, 0, w, 0, M, N, K, bias, mult, 36, True, site, out=y))
+    t_s32 = time_kernel(lambda: _ops.gemm_s32(x, 0, w, 0, M, N, K))
+    t_cublas = time_kernel(lambda: torch._int_mm(x, w.t()))
+    ops = 2.0 * M * N * K
+    return {"shape": [M, N, K], "fused_requant_tops": ops / t_fused / 1e12, "fused_ms": t_fused * 1e3,
+            "s32_tops": ops / t_s32 / 1e12, "torch_int_mm_cublas_tops": ops / t_cublas / 1e12}, t_fused, ops
+
+
+def eco_step_measurement(device, layers=64, dim=4096, steps=5):
+    """Config 4: I8ECO.step over 64 x 4096^2 int8 parameters (w, m, g uniform in [-127, 127])."""
+    from ecoint8 import I8ECO, _ops
+
+    gen = torch.Generator(device=device).manual_seed(2)
+    proto = fast_layer(dim, dim, gen, device)
+    lys = []
+    for _ in range(layers):
+        lin = fast_layer(1, 1, gen, device)
+        lin.w_i8 = torch.randint(-127, 128, (dim, dim), dtype=torch.int8, device=device, generator=gen)
+        lin.b_acc = torch.zeros(dim, dtype=torch.int32, device=device)
+        lin.sw = list(proto.sw)
+        lin.sx = 0.01
+        lin._gw_i8 = torch.randint(-127, 128, (dim, dim), dtype=torch.int8, device=device, generator=gen)
+        lin._gw_s = 2e-4
+        lin._gw_sumsq = _ops.sumsq(lin._gw_i8)  # produced by the dW requant in training
+        lin._gw_sumsq_of = lin._gw_i8
+        lin._gb_sum = torch.randint(-10 ** 6, 10 ** 6, (dim,), dtype=torch.int64, device=device, generator=gen)
+        lin._gb_s = 1e-4
+        lys.append(lin)
+    opt = I8ECO(lys, lr=0.05, momentum=0.9)
+    for m in opt.m_i8:
+        m.copy_(torch.randint(-127, 128, m.shape, dtype=torch.int8, device=device, generator=gen))
+    opt.s_m = [3e-4] * layers
+    t = time_kernel(opt.step, iters=steps, warmup=3)
+    params = layers * dim * dim
+    return {"params": params, "bytes_per_param": 5, "ms": t * 1e3, "gbs": 5.0 * params / t / 1e9}
+
+
+def cpu_baseline_port():
+    """The oracle port of the reference strict step on the host cores, on a bounded sample.
+
+    Each part of one 8192->8192 layer is timed on a sample and scaled by its own
+    work to the full config-5 step (9 layers, batch 16384):
+    forward and dX (GEMM + requant) at batch 256 -> x 64; the dW GEMM on 256 output
+    rows at batch 256 -> x 32 x 64; the dW requant and the I8ECO step on 256 rows -> x 32.
+    """
+    import numpy as np
+
+    from oracle import fixedpoint as ofp
+    from oracle import strict as ost
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(0)
+    d, b, rows = 8192, 256, 256
+    w = rng.integers(-127, 128, (d, d), dtype=np.int8)
+    x = rng.integers(-127, 128, (b, d), dtype=np.int8)
+    g = rng.integers(-127, 128, (b, d), dtype=np.int8)
+    wf = w.astype(np.float64)  # the port's exact GEMM format (ofp.int_mm), converted once per step
+    sw = [1e-2 + 1e-6 * i for i in range(d)]
+    draw = ost.TorchDraws()
+
+    def mm(a, bf):  # ofp.int_mm with the right operand already in float64
+        return (a.astype(np.float64) @ bf).astype(np.int64).astype(np.int32)
+
+    t0 = time.perf_counter()
+    ost.common_shift_requant(mm(x, wf.T), [0.02 * s / 0.5 for s in sw], draw)  # forward
+    dx = mm(g, wf)
+    m, sh = ofp.quantize_multiplier(1e-4)
+    ofp.to_int8_sat(ofp.apply_mult_shift(dx, m, sh, True, draw(dx.shape, 1 << sh)))  # dX
+    t_batch = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    dw = ofp.int_mm(g[:, :rows].T, x)  # dW rows, K = batch sample
+    t_dw = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    gw = ofp.to_int8_sat(ofp.apply_mult_shift(dw, m, sh, True, draw(dw.shape, 1 << sh)))
+    sub = ost.I8Linear(w[:rows].copy(), sw[:rows])
+    sub.sx = 0.02
+    sub._gw_i8, sub._gw_s = gw, 3e-5
+    sub._gb_sum, sub._gb_s = g[:, :rows].astype(np.int64).sum(0), 3e-5
+    ost.I8ECO([sub], lr=0.05).step(draw)
+    t_rows = time.perf_counter() - t0
+    layer_equiv = sum(a * o for a, o in LAYERS) / (d * d)
+    t_full = layer_equiv * (t_batch * GLOBAL_BATCH / b + t_dw * (d / rows) * (GLOBAL_BATCH / b)
+                            + t_rows * d / rows)
+    return {"value": 1.0 / t_full, "unit": "steps/s", "cores": threads, "kind": "port",
+            "sample": f"numpy oracle port of one 8192x8192 layer: fwd+dX at batch {b} ({t_batch:.2f} s), dW GEMM "
+                      f"{rows} rows x batch {b} ({t_dw:.2f} s), dW requant + I8ECO step on {rows} rows "
+                      f"({t_rows:.2f} s); scaled by work to 9 layers x batch {GLOBAL_BATCH}",
+            "seconds_per_step_estimate": t_full}
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus > 1 and world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} needs torchrun with {args.gpus} ranks (WORLD_SIZE={world})")
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        vals = []
+        for _ in range(args.warmup):
+            cpu_baseline_port()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            vals.append(cpu_baseline_port())
+        el = time.perf_counter() - t0
+        v = statistics.median(x["value"] for x in vals)
+        cb = dict(vals[-1])
+        cb["value"] = v
+        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "steps/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "strong",
+                          "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+                          "config": {"workload": "config 5 deep MLP", "global_batch": GLOBAL_BATCH,
+                                     "parallelism": f"dp{args.gpus}", "sampled_wall_s": el},
+                          "cpu_baseline": cb,
+                          "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    from ecoint8 import I8ECO, parallel
+    from ecoint8._sr import batch_rows, set_generator
+
+    if world > 1:
+        parallel.init()
+    set_generator(torch.Generator().manual_seed(1234))  # identical Philox keys on every rank
+    local_b = GLOBAL_BATCH // world
+    torch.manual_seed(0)
+    net = build_mlp(device)
+    gen = torch.Generator(device=device).manual_seed(100 + rank)
+    x_fp = torch.randn(local_b, LAYERS[0][0], device=device, generator=gen)
+    y = torch.randint(0, LAYERS[-1][1], (local_b,), device=device, generator=gen)
+    from ecoint8.quant import quantize_tensor_dynamic
+
+    with batch_rows(rank * local_b):
+        x0, sx0 = quantize_tensor_dynamic(x_fp)
+        net.calibrate(x0, sx0)
+        x_i8 = net.quantize_input(x_fp)[0]
+        del x_fp, x0
+        opt = I8ECO(net.int8_layers(), lr=0.05, momentum=0.9)
+
+        def barrier():
+            if world > 1:
+                torch.distributed.barrier()
+
+        for _ in range(args.warmup):
+            train_step(net, opt, x_i8, y, world)
+        torch.cuda.synchronize()
+        barrier()
+        counter = LaunchCounter()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk, counter:
+            torch.cuda.synchronize()
+            barrier()
+            ev0.record()
+            for _ in range(args.steps):
+                train_step(net, opt, x_i8, y, world)
+            ev1.record()
+            torch.cuda.synchronize()
+            barrier()
+        ms = ev0.elapsed_time(ev1)
+        launches = counter.count // args.steps
+        # e2e: the same steps through the public API with the int8 batch and labels coming
+        # from pinned host memory and the loss read back every step
+        x_host = x_i8.cpu().pin_memory()
+        y_host = y.cpu().pin_memory()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            xb = x_host.to(device, non_blocking=True)
+            yb = y_host.to(device, non_blocking=True)
+            loss = train_step(net, opt, xb, yb, world)
+            float(loss.item())
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_e2e = t.tolist()
+    value = args.steps / (ms / 1e3)
+    e2e = args.steps / (ms_e2e / 1e3)
+    out = None
+    if rank == 0:
+        hbm, bf16, src = _peaks()
+        int8_peak = 2.0 * bf16  # dense int8 = 2x dense bf16 on B200 (no measured int8 peak)
+        out = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+               "scaling": "strong", "vs_baseline": None, "dtype": "int8/int32/int64", "data": "synthetic",
+               "config": {"workload": "config 5: deep strict-int8 MLP 8x I8Linear(8192,8192)+I8ReLU, "
+                                      "I8Linear(8192,1000); Gaussian inputs, random labels; I8ECO momentum 0.9",
+                          "global_batch": GLOBAL_BATCH, "per_gpu_batch": local_b, "parallelism": f"dp{world}",
+                          "l2": "inputs larger than L2 (1.2 GB activations + 0.55 GB weights); no flush"},
+               "e2e": {"value": e2e, "unit": "steps/s", "h2d_bytes_per_step": int(x_i8.numel() + y.numel() * 8),
+                       "d2h_bytes_per_step": 4},
+               "gpu_launches": launches, "clocks": clk.summary()}
+        if world == 1 and not args.no_side:
+            gm, t_fused, ops = gemm_measurements(device)
+            out["gemm"] = gm
+            out["eco_step"] = eco_step_measurement(device)
+            achieved = ops / t_fused / 1e12
+            out["roofline"] = {"bound": "tensor", "kernel": "gemm_s8_kernel<256,1> (fused forward, 16384x8192x8192)",
+                               "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
+                               "peak_source": f"2 x {src} bf16 dense ({bf16} TFLOP/s)",
+                               "frac": achieved / int8_peak, "traffic": _traffic()}
+            out["eco_step"]["frac_of_hbm"] = out["eco_step"]["gbs"] / hbm
+            out["cpu_baseline"] = {k: v for k, v in cpu_baseline_port().items() if k != "seconds_per_step_estimate"}
+        print(json.dumps(out))
+    if world > 1:
+        parallel.shutdown()
+        torch.distributed.destroy_process_group()
+
+
+def _traffic():
+    """DRAM bytes per launch of the roofline kernel, from the committed ncu summary (or None)."""
+    p = REPO / "profiles" / "gemm_fwd_fused_16384x8192x8192.md"
+    if p.exists():
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    return None
+
+
+if __name__ == "__main__":
+    main()

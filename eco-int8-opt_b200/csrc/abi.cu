@@ -1,0 +1,62 @@
+// C-ABI housekeeping: version, last error, device support, shared checks.
+#include "abi.cuh"
+
+#include <cstring>
+#include <mutex>
+
+static thread_local char g_last_error[512] = "";
+
+int eco_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int eco_launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return eco_fail(ECO_ERR_LAUNCH, "%s: %s", what, cudaGetErrorString(e));
+  return ECO_OK;
+}
+
+int eco_num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int eco_check_sr(const eco_sr_t& sr, int shift, const char* who) {
+  if (shift > 62)
+    return eco_fail(ECO_ERR_RANGE, "%s: shift %d > 62 does not fit the int64 requant", who, shift);
+  if (sr.mode < ECO_SR_NEAREST || sr.mode > ECO_SR_REPLAY64)
+    return eco_fail(ECO_ERR_ARG, "%s: unknown SR mode %d", who, sr.mode);
+  if ((sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64) && shift >= 0 && sr.nudge == nullptr)
+    return eco_fail(ECO_ERR_ARG, "%s: replay SR mode without a nudge tensor", who);
+  return ECO_OK;
+}
+
+extern "C" int eco_abi_version(void) { return ECO_ABI_VERSION; }
+
+extern "C" const char* eco_last_error(void) { return g_last_error; }
+
+extern "C" int eco_device_supported(int device) {
+  int major = 0, minor = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) {
+    cudaGetLastError();
+    return eco_fail(ECO_ERR_ARG, "eco_device_supported: no CUDA device %d", device);
+  }
+  return (major == 10 && minor == 0) ? 1 : 0;
+}
+
+extern "C" int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_t ld_dst,
+                             int64_t rows, int64_t cols, eco_stream_t stream) {
+  ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && ld_src >= cols && ld_dst >= cols, ECO_ERR_ARG,
+              "eco_copy2d_s8: bad arguments");
+  if (rows == 0 || cols == 0) return ECO_OK;
+  cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)ld_dst, src, (size_t)ld_src, (size_t)cols, (size_t)rows,
+                                    cudaMemcpyDeviceToDevice, eco_stream(stream));
+  if (e != cudaSuccess) return eco_fail(ECO_ERR_LAUNCH, "eco_copy2d_s8: %s", cudaGetErrorString(e));
+  return ECO_OK;
+}

@@ -1,0 +1,116 @@
+// Shared device helpers for the ecoint8 B200 library (sm_100a).
+//
+// Integer semantics follow PyTorch's int64 kernels, which the reference's
+// strict path runs on (ecoint8/fixedpoint.py): products and sums wrap modulo
+// 2^64, `a << s` is an unsigned shift that yields 0 for s >= 64, `a >> s` is
+// arithmetic and saturates to the sign for s >= 64, and a floor division by
+// 2^s is an arithmetic right shift.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/ecoint8_b200.h"
+
+typedef long long i64;
+typedef unsigned long long u64;
+
+#define ECO_DEV __device__ __forceinline__
+
+// ---------------------------------------------------------------- int64 wrap
+ECO_DEV i64 mul64(i64 a, i64 b) { return (i64)((u64)a * (u64)b); }
+ECO_DEV i64 add64(i64 a, i64 b) { return (i64)((u64)a + (u64)b); }
+ECO_DEV i64 sub64(i64 a, i64 b) { return (i64)((u64)a - (u64)b); }
+ECO_DEV i64 neg64(i64 a) { return (i64)(0ull - (u64)a); }
+ECO_DEV i64 abs64(i64 a) { return a < 0 ? neg64(a) : a; }  // torch abs: INT64_MIN stays
+ECO_DEV i64 shl64(i64 a, int s) { return s >= 64 ? 0 : (i64)((u64)a << s); }
+ECO_DEV i64 sar64(i64 a, int s) { return a >> (s > 63 ? 63 : s); }
+ECO_DEV int add32(int a, int b) { return (int)((unsigned)a + (unsigned)b); }
+ECO_DEV int8_t sat8(i64 v) { return (int8_t)(v < -127 ? -127 : (v > 127 ? 127 : v)); }
+
+// `apply_mult_shift` (fixedpoint.py:52-76) on one element: shift >= 0 rounds
+// with `nudge` (either a U[0, 2^shift) draw or 2^(shift-1)); shift < 0 is a
+// left shift with no draw.
+ECO_DEV i64 ams(i64 x, i64 mult, int shift, i64 nudge) {
+  i64 p = mul64(x, mult);
+  return shift >= 0 ? sar64(add64(p, nudge), shift) : shl64(p, -shift);
+}
+ECO_DEV i64 half_nudge(int shift) { return shift > 0 ? (1ll << (shift - 1)) : 0; }
+ECO_DEV i64 low_bits(u64 w, int n) { return n <= 0 ? 0 : (n >= 64 ? (i64)w : (i64)(w & ((1ull << n) - 1))); }
+
+// ---------------------------------------------------------------- Philox4x32-10
+// Salmon et al., "Parallel random numbers: as easy as 1, 2, 3" (SC'11).
+struct Philox4 {
+  uint32_t x, y, z, w;
+};
+ECO_DEV Philox4 philox10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const u64 p0 = (u64)0xD2511F53u * c0;
+    const u64 p1 = (u64)0xCD9E8D57u * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1;
+    c1 = (uint32_t)p1;
+    c3 = (uint32_t)p0;
+    c0 = n0;
+    c2 = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return Philox4{c0, c1, c2, c3};
+}
+
+// The library's stochastic-rounding stream: 64 random bits for the column
+// pair (2p, 2p+1) of row r at site `stream`: counter (p, r, stream_lo,
+// stream_hi), key (seed_lo, seed_hi).  Even column -> (y:x), odd -> (w:z).
+ECO_DEV void sr_pair(u64 seed, u64 stream, uint32_t row, uint32_t pair, u64& even, u64& odd) {
+  const Philox4 o = philox10(pair, row, (uint32_t)stream, (uint32_t)(stream >> 32), (uint32_t)seed,
+                             (uint32_t)(seed >> 32));
+  even = ((u64)o.y << 32) | o.x;
+  odd = ((u64)o.w << 32) | o.z;
+}
+ECO_DEV u64 sr_word(u64 seed, u64 stream, uint32_t row, uint32_t col) {
+  u64 e, o;
+  sr_pair(seed, stream, row, col >> 1, e, o);
+  return (col & 1) ? o : e;
+}
+
+// Triton's tl.rand(seed, offset) for an int32 offset: Philox counter
+// (offset, 0, 0, 0); first word as int32, folded to non-negative, times fp32
+// 4.6566127342e-10 (triton/language/random.py, triton 3.6.0).
+ECO_DEV float tl_rand(u64 seed, uint32_t offset) {
+  const Philox4 o = philox10(offset, 0u, 0u, 0u, (uint32_t)seed, (uint32_t)(seed >> 32));
+  int x = (int)o.x;
+  x = x < 0 ? -x - 1 : x;
+  return __fmul_rn(__int2float_rn(x), 4.6566127342e-10f);
+}
+
+// ---------------------------------------------------------------- fixed point
+// quantize_multiplier (fixedpoint.py:26-37) in IEEE double: frexp is exact,
+// mantissa * 2^31 is exact, and rint rounds half to even like Python's round.
+ECO_DEV void qmult(double r, int& mult, int& shift) {
+  if (r == 0.0) {
+    mult = 0;
+    shift = 0;
+    return;
+  }
+  int e;
+  const double mant = frexp(r, &e);
+  i64 m = (i64)rint(__dmul_rn(mant, 2147483648.0));
+  if (m == (1ll << 31)) {
+    m >>= 1;
+    e += 1;
+  }
+  mult = (int)m;
+  shift = 31 - e;
+}
+
+// Error flags a kernel can raise in its error word (host turns them into exceptions).
+enum : unsigned {
+  ECO_FLAG_SHIFT_OVERFLOW = 1u,  // a requant shift beyond 62 (the reference raises)
+  ECO_FLAG_BAD_RATIO = 2u,       // a zero / non-finite scale ratio
+  ECO_FLAG_WAIT_TIMEOUT = 4u,    // a bounded device wait gave up
+};
+
+// ---------------------------------------------------------------- misc
+static inline int eco_ceil_div(i64 a, i64 b) { return (int)((a + b - 1) / b); }

@@ -1,0 +1,338 @@
+// Fused single-pass integer ECO-SGDM step over many layers (I8ECO.step,
+// ecoint8/strict/iopt.py:103-200), one launch, no host synchronisation.
+//
+// Layout: each layer's w, m, g are [rows, cols] int8 row-major in HBM.  The
+// launch walks "tiles" of whole rows (rows_per_tile rows of one layer); a
+// warp owns one row at a time and streams it with 16-byte loads, so the per-
+// row fixed-point multipliers (iopt.py:134-148) are computed once per row in
+// IEEE double and every element is one pass of int64 register arithmetic:
+// read w, m, g (3 B) and write w, m (2 B).
+//
+// The common shift of a multiplier column is min over rows of the row shift;
+// quantize_multiplier's shift is non-increasing in the ratio and each ratio is
+// monotone in sw[o], so the common shift is the shift of the ratio at min(sw)
+// (or max(sw) for the momentum requant column), computed per CTA in O(1).
+//
+// The new momentum scale (iopt.py:178-180) needs max over rows of
+// rowmax_o * sw_o / 4096: every warp folds its rows into a CTA maximum, one
+// atomicMax per CTA on the double's bits (non-negative doubles order like
+// their bit patterns), and the last CTA to finish turns it into s_m and resets
+// the accumulator and the completion counter for the next step.
+#include <algorithm>
+
+#include "abi.cuh"
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxLayers = 80;  // per launch (kernel parameter space)
+
+struct LayerDesc {
+  eco_i8eco_layer_t L;
+  i64 tile_begin;
+  int rows_per_tile;
+  int vec;  // cols % 16 == 0 and 16-byte aligned rows
+};
+
+struct StepParams {
+  eco_i8eco_hyper_t H;
+  int n_layers;
+  i64 total_tiles;
+  LayerDesc layers[kMaxLayers];
+};
+
+struct LayerScalars {
+  double s_m, sm4096, sg4096, lr_sgb;
+  int com_m, com_g, com_mm, com_b;
+  unsigned flags;
+};
+
+ECO_DEV double bits_to_double(i64 b) { return __longlong_as_double(b); }
+
+ECO_DEV int shift_of(double r, unsigned& flags) {
+  if (!(r >= 0.0) || r > 1.7e308) {  // NaN, negative or infinite ratio
+    flags |= ECO_FLAG_BAD_RATIO;
+    return 0;
+  }
+  int m, s;
+  qmult(r, m, s);
+  return s;
+}
+
+ECO_DEV LayerScalars layer_scalars(const eco_i8eco_layer_t& L, const eco_i8eco_hyper_t& H) {
+  LayerScalars S;
+  S.flags = 0;
+  double s_g = L.s_g;
+  if (H.grad_clip >= 0.0) {  // iopt.py:90-101
+    const i64 sq = *L.gsq;
+    const double n_real = __dmul_rn(__dsqrt_rn(__ll2double_rn(sq)), s_g);
+    if (n_real > H.grad_clip) s_g = __dmul_rn(s_g, __ddiv_rn(H.grad_clip, n_real));
+  }
+  S.s_m = bits_to_double(L.state[0]);
+  S.sm4096 = __dmul_rn(S.s_m, 4096.0);
+  S.sg4096 = __dmul_rn(s_g, 4096.0);
+  S.com_m = shift_of(__ddiv_rn(S.sm4096, L.sw_min), S.flags);
+  S.com_g = shift_of(__ddiv_rn(S.sg4096, L.sw_min), S.flags);
+  S.com_mm = S.s_m > 0.0 ? shift_of(__ddiv_rn(__ddiv_rn(L.sw_max, 4096.0), S.s_m), S.flags) : 0;
+  S.lr_sgb = __dmul_rn(H.lr, L.s_gb);
+  S.com_b = L.b_acc ? shift_of(__ddiv_rn(S.lr_sgb, __dmul_rn(L.sx, L.sw_min)), S.flags) : 0;
+  if (S.com_m > 62 || S.com_g > 62 || S.com_mm > 62 || S.com_b > 62) S.flags |= ECO_FLAG_SHIFT_OVERFLOW;
+  return S;
+}
+
+// Row multiplier m_o >> (s_o - com) (ilayer.py:68 / iopt.py:53).
+ECO_DEV i64 row_mult(double r, int com, unsigned& flags) {
+  if (!(r >= 0.0) || r > 1.7e308) {
+    flags |= ECO_FLAG_BAD_RATIO;
+    return 0;
+  }
+  int m, s;
+  qmult(r, m, s);
+  if (s < com) {
+    flags |= ECO_FLAG_BAD_RATIO;
+    return 0;
+  }
+  const int d = s - com;
+  return d >= 31 ? 0 : (i64)(m >> d);
+}
+
+struct RowCtx {
+  i64 mult_m, mult_g, mult_mm;
+  int com_m, com_g, com_mm;
+  i64 half_m, half_g;
+  i64 b_q, nb_q, lr_q, a_q;
+};
+
+// One element of iopt.py:154-176.  Returns new w, new m (int8) and updates row stats.
+ECO_DEV void eco_elem(const RowCtx& c, int w, int m, int g, i64 nw, i64 nm, int8_t& w8, int8_t& m8,
+                      i64& rmax, u64& rsum) {
+  const i64 mU = ams(m, c.mult_m, c.com_m, c.half_m);
+  const i64 gU = ams(g, c.mult_g, c.com_g, c.half_g);
+  const i64 m_t = sar64(add64(mul64(mU, c.b_q), mul64(gU, c.nb_q)), 16);
+  const i64 thU = sub64((i64)w << 12, sar64(mul64(m_t, c.lr_q), 16));
+  i64 wn = sar64(add64(thU, nw), 12);
+  wn = wn < -127 ? -127 : (wn > 127 ? 127 : wn);
+  const i64 eU = sub64(thU, wn << 12);
+  const i64 m_new = add64(m_t, sar64(mul64(eU, c.a_q), 16));
+  rmax = max(rmax, abs64(m_new));
+  rsum += (u64)abs64(eU);
+  w8 = (int8_t)wn;
+  m8 = sat8(ams(m_new, c.mult_mm, c.com_mm, nm));
+}
+
+ECO_DEV i64 replay(const void* p, int bits, i64 idx) {
+  return bits == 32 ? (i64)static_cast<const int32_t*>(p)[idx] : static_cast<const i64*>(p)[idx];
+}
+
+// Weight and momentum nudges of one element pair (c even), Philox mode.
+ECO_DEV void philox_nudges(u64 seed, u64 stream, uint32_t row, uint32_t c, int com_mm, i64 (&nw)[2],
+                           i64 (&nm)[2]) {
+  u64 w0, w1;
+  sr_pair(seed, stream, row, c >> 1, w0, w1);
+  nw[0] = (i64)(w0 & 0xFFF);
+  nw[1] = (i64)(w1 & 0xFFF);
+  if (com_mm < 0) {
+    nm[0] = nm[1] = 0;
+  } else if (com_mm <= 52) {
+    nm[0] = low_bits(w0 >> 12, com_mm);
+    nm[1] = low_bits(w1 >> 12, com_mm);
+  } else {
+    u64 a0, a1;
+    sr_pair(seed, stream | (1ull << 63), row, c >> 1, a0, a1);
+    nm[0] = low_bits(a0, com_mm);
+    nm[1] = low_bits(a1, com_mm);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_constant__ StepParams P) {
+  __shared__ double s_wmax[kWarps];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const eco_i8eco_hyper_t& H = P.H;
+  for (i64 t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
+    int li = 0;
+    while (li + 1 < P.n_layers && P.layers[li + 1].tile_begin <= t) ++li;
+    const LayerDesc& D = P.layers[li];
+    const eco_i8eco_layer_t& L = D.L;
+    const LayerScalars S = layer_scalars(L, H);
+    if (S.flags) {  // the reference raises here: leave the layer untouched, flag it
+      if (threadIdx.x == 0) atomicOr(reinterpret_cast<unsigned long long*>(&L.state[2]), (u64)S.flags);
+      continue;
+    }
+    const i64 r0 = (t - D.tile_begin) * D.rows_per_tile;
+    const i64 r1 = min((i64)L.rows, r0 + (i64)D.rows_per_tile);
+    double wmax = 0.0;
+    unsigned flags = 0;
+    for (i64 r = r0 + warp; r < r1; r += kWarps) {
+      const double sw_o = L.sw[r];
+      RowCtx c;
+      c.com_m = S.com_m;
+      c.com_g = S.com_g;
+      c.com_mm = S.com_mm;
+      c.half_m = half_nudge(S.com_m);
+      c.half_g = half_nudge(S.com_g);
+      c.b_q = H.b_q;
+      c.nb_q = H.nb_q;
+      c.lr_q = H.lr_q;
+      c.a_q = H.a_q;
+      c.mult_m = row_mult(__ddiv_rn(S.sm4096, sw_o), S.com_m, flags);
+      c.mult_g = row_mult(__ddiv_rn(S.sg4096, sw_o), S.com_g, flags);
+      c.mult_mm = S.s_m > 0.0 ? row_mult(__ddiv_rn(__ddiv_rn(sw_o, 4096.0), S.s_m), S.com_mm, flags) : 0;
+      i64 rmax = INT64_MIN;
+      u64 rsum = 0;
+      int8_t* wr = L.w + r * L.cols;
+      int8_t* mr = L.m + r * L.cols;
+      const int8_t* gr = L.g + r * L.cols;
+      const bool philox = H.sr_mode == ECO_SR_PHILOX;
+      if (D.vec) {
+        for (i64 j = lane; j < L.cols / 16; j += 32) {
+          const i64 c0 = j * 16;
+          int4 wv = *reinterpret_cast<const int4*>(wr + c0);
+          int4 mv = *reinterpret_cast<const int4*>(mr + c0);
+          const int4 gv = *reinterpret_cast<const int4*>(gr + c0);
+          int8_t* wb = reinterpret_cast<int8_t*>(&wv);
+          int8_t* mb = reinterpret_cast<int8_t*>(&mv);
+          const int8_t* gb = reinterpret_cast<const int8_t*>(&gv);
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            i64 nw[2], nm[2];
+            if (philox) {
+              philox_nudges(H.seed, L.stream_w, (uint32_t)r, (uint32_t)(c0 + e), S.com_mm, nw, nm);
+            } else {
+              const i64 idx = r * L.cols + c0 + e;
+              nw[0] = replay(L.nudge_w, 32, idx);
+              nw[1] = replay(L.nudge_w, 32, idx + 1);
+              nm[0] = S.com_mm >= 0 ? replay(L.nudge_m, L.nudge_m_bits, idx) : 0;
+              nm[1] = S.com_mm >= 0 ? replay(L.nudge_m, L.nudge_m_bits, idx + 1) : 0;
+            }
+            eco_elem(c, wb[e], mb[e], gb[e], nw[0], nm[0], wb[e], mb[e], rmax, rsum);
+            eco_elem(c, wb[e + 1], mb[e + 1], gb[e + 1], nw[1], nm[1], wb[e + 1], mb[e + 1], rmax, rsum);
+          }
+          *reinterpret_cast<int4*>(wr + c0) = wv;
+          *reinterpret_cast<int4*>(mr + c0) = mv;
+        }
+      } else {
+        for (i64 c0 = 2 * lane; c0 < L.cols; c0 += 64) {
+          i64 nw[2], nm[2];
+          if (philox) {
+            philox_nudges(H.seed, L.stream_w, (uint32_t)r, (uint32_t)c0, S.com_mm, nw, nm);
+          }
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const i64 col = c0 + e;
+            if (col >= L.cols) break;
+            if (!philox) {
+              const i64 idx = r * L.cols + col;
+              nw[e] = replay(L.nudge_w, 32, idx);
+              nm[e] = S.com_mm >= 0 ? replay(L.nudge_m, L.nudge_m_bits, idx) : 0;
+            }
+            int8_t w8, m8;
+            eco_elem(c, wr[col], mr[col], gr[col], nw[e], nm[e], w8, m8, rmax, rsum);
+            wr[col] = w8;
+            mr[col] = m8;
+          }
+        }
+      }
+      // row reductions (torch: abs().amax(1), abs().sum(1) on int64)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        rmax = max(rmax, (i64)__shfl_xor_sync(0xffffffffu, rmax, o));
+        rsum += __shfl_xor_sync(0xffffffffu, rsum, o);
+      }
+      if (lane == 0) {
+        if (L.rowsum) L.rowsum[r] = (i64)rsum;
+        // r * sw_o / 4096 (iopt.py:178); a negative row max can only come from INT64_MIN
+        const double v = __ddiv_rn(__dmul_rn(__ll2double_rn(rmax), sw_o), 4096.0);
+        wmax = fmax(wmax, v);
+        if (L.b_acc) {  // bias integer SGD (iopt.py:187-197)
+          const i64 mb = row_mult(__ddiv_rn(S.lr_sgb, __dmul_rn(L.sx, sw_o)), S.com_b, flags);
+          i64 nb = 0;
+          if (S.com_b >= 0) {
+            nb = philox ? low_bits(sr_word(H.seed, L.stream_b, (uint32_t)r, 0u), S.com_b)
+                        : replay(L.nudge_b, L.nudge_b_bits, r);
+          }
+          const int delta = (int)ams(L.gb_sum[r], mb, S.com_b, nb);
+          L.b_acc[r] = (int)((unsigned)L.b_acc[r] - (unsigned)delta);
+        }
+      }
+    }
+    if (flags && lane == 0) atomicOr(reinterpret_cast<unsigned long long*>(&L.state[2]), (u64)flags);
+    if (lane == 0) s_wmax[warp] = wmax;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double v = 0.0;
+      for (int w = 0; w < kWarps; ++w) v = fmax(v, s_wmax[w]);
+      if (v > 0.0)
+        atomicMax(reinterpret_cast<unsigned long long*>(&L.state[1]), (u64)__double_as_longlong(v));
+    }
+    __syncthreads();
+  }
+  // the last CTA to finish publishes the new momentum scales (iopt.py:178-180)
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(H.done_counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int li = threadIdx.x; li < P.n_layers; li += blockDim.x) {
+    i64* st = reinterpret_cast<i64*>(P.layers[li].L.state);
+    const i64 acc = atomicExch(reinterpret_cast<unsigned long long*>(&st[1]), 0ull);
+    const u64 fl = atomicAdd(reinterpret_cast<unsigned long long*>(&st[2]), 0ull);
+    if (fl) continue;  // flagged layer keeps its scale
+    const double amax_real = __longlong_as_double(acc);
+    const double s_m_new = amax_real > 0.0 ? __ddiv_rn(amax_real, 127.0) : 1.0;
+    st[0] = __double_as_longlong(s_m_new);
+  }
+  if (threadIdx.x == 0) *H.done_counter = 0u;
+}
+
+}  // namespace
+
+extern "C" int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, const eco_i8eco_hyper_t* hyper,
+                              eco_stream_t stream) {
+  ECO_REQUIRE(layers && hyper && n_layers >= 0, ECO_ERR_ARG, "eco_i8eco_step: bad arguments");
+  ECO_REQUIRE(hyper->done_counter, ECO_ERR_ARG, "eco_i8eco_step: done_counter is required");
+  ECO_REQUIRE(hyper->sr_mode == ECO_SR_PHILOX || hyper->sr_mode == ECO_SR_REPLAY32 ||
+                  hyper->sr_mode == ECO_SR_REPLAY64,
+              ECO_ERR_ARG, "eco_i8eco_step: sr_mode must be Philox or replay");
+  const bool replay = hyper->sr_mode != ECO_SR_PHILOX;
+  for (int i = 0; i < n_layers; ++i) {
+    const eco_i8eco_layer_t& L = layers[i];
+    ECO_REQUIRE(L.w && L.m && L.g && L.sw && L.state && L.rows > 0 && L.cols > 0, ECO_ERR_ARG,
+                "eco_i8eco_step: layer %d: null tensor or empty shape", i);
+    ECO_REQUIRE(L.rows < (1ll << 31) && L.cols < (1ll << 31), ECO_ERR_ARG, "eco_i8eco_step: layer %d too large", i);
+    ECO_REQUIRE(hyper->grad_clip < 0.0 || L.gsq, ECO_ERR_ARG, "eco_i8eco_step: layer %d: clipping needs gsq", i);
+    ECO_REQUIRE(!L.b_acc || L.gb_sum, ECO_ERR_ARG, "eco_i8eco_step: layer %d: bias needs gb_sum", i);
+    ECO_REQUIRE(!replay || (L.nudge_w && L.nudge_m && (!L.b_acc || L.nudge_b)), ECO_ERR_ARG,
+                "eco_i8eco_step: layer %d: replay mode needs nudge tensors", i);
+    ECO_REQUIRE(!replay || ((L.nudge_m_bits == 32 || L.nudge_m_bits == 64) &&
+                            (!L.b_acc || L.nudge_b_bits == 32 || L.nudge_b_bits == 64)),
+                ECO_ERR_ARG, "eco_i8eco_step: layer %d: nudge widths", i);
+  }
+  cudaStream_t s = eco_stream(stream);
+  static_assert(sizeof(StepParams) < 30000, "kernel parameter space");
+  for (int base = 0; base < n_layers; base += kMaxLayers) {
+    StepParams P;
+    P.H = *hyper;
+    P.n_layers = std::min(kMaxLayers, n_layers - base);
+    i64 tiles = 0;
+    for (int i = 0; i < P.n_layers; ++i) {
+      LayerDesc& D = P.layers[i];
+      D.L = layers[base + i];
+      const i64 target = std::max<i64>(kWarps, (64 * 1024) / D.L.cols);
+      D.rows_per_tile = (int)std::min<i64>(D.L.rows, (target + kWarps - 1) / kWarps * kWarps);
+      D.tile_begin = tiles;
+      D.vec = (D.L.cols % 16 == 0) && eco_aligned16(D.L.w) && eco_aligned16(D.L.m) && eco_aligned16(D.L.g);
+      tiles += (D.L.rows + D.rows_per_tile - 1) / D.rows_per_tile;
+    }
+    P.total_tiles = tiles;
+    int occ = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, i8eco_step_kernel, kThreads, 0);
+    const i64 grid = std::max<i64>(1, std::min<i64>(tiles, (i64)eco_num_sms() * std::max(occ, 1)));
+    i8eco_step_kernel<<<(unsigned)grid, kThreads, 0, s>>>(P);
+    if (int rc = eco_launch_check("eco_i8eco_step")) return rc;
+  }
+  return ECO_OK;
+}

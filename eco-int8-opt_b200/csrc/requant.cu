@@ -1,0 +1,295 @@
+// Memory-bound integer kernels of the strict path: int32 -> int8 requant with
+// fused bias / ReLU / mask / square-sum, the general apply_mult_shift, column
+// sums, max-abs and square-sum reductions.
+#include <algorithm>
+
+#include "abi.cuh"
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T>
+ECO_DEV T warp_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+ECO_DEV i64 warp_max64(i64 v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, (i64)__shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide reduction of one int64 into a global word (sum or max).
+template <bool MAX>
+ECO_DEV void block_reduce_to(i64 v, i64* out) {
+  __shared__ i64 part[kThreads / 32];
+  v = MAX ? warp_max64(v) : (i64)warp_sum((u64)v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) part[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? part[lane] : (MAX ? (i64)INT64_MIN : 0);
+    v = MAX ? warp_max64(v) : (i64)warp_sum((u64)v);
+    if (lane == 0) {
+      if (MAX)
+        atomicMax(reinterpret_cast<long long*>(out), (long long)v);
+      else
+        atomicAdd(reinterpret_cast<unsigned long long*>(out), (unsigned long long)v);
+    }
+  }
+}
+
+ECO_DEV i64 replay_nudge(const eco_sr_t& sr, i64 r, i64 c) {
+  const i64 idx = r * sr.nudge_ld + c;
+  return sr.mode == ECO_SR_REPLAY32 ? (i64)(static_cast<const int32_t*>(sr.nudge)[idx])
+                                    : static_cast<const i64*>(sr.nudge)[idx];
+}
+
+// Nudges for 16 consecutive columns c0..c0+15 (c0 even) of row r.
+ECO_DEV void nudges16(const eco_sr_t& sr, int shift, i64 r, i64 c0, i64 cols, i64 (&n)[16]) {
+  if (shift < 0) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) n[e] = 0;
+  } else if (sr.mode == ECO_SR_NEAREST) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) n[e] = half_nudge(shift);
+  } else if (sr.mode == ECO_SR_PHILOX) {
+    const uint32_t row = (uint32_t)(sr.row_base + r);
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      u64 we, wo;
+      sr_pair(sr.seed, sr.stream, row, (uint32_t)((c0 + e) >> 1), we, wo);
+      n[e] = low_bits(we, shift);
+      n[e + 1] = low_bits(wo, shift);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) n[e] = (c0 + e < cols) ? replay_nudge(sr, r, c0 + e) : 0;
+  }
+}
+
+struct RequantArgs {
+  const int32_t* src;
+  i64 rows, cols, ld_src;
+  const int32_t* bias;
+  const int32_t* mult_col;
+  i64 mult_scalar;
+  int shift, relu;
+  eco_sr_t sr;
+  const int8_t* mask;
+  i64 ld_mask;
+  int8_t* dst;
+  i64 ld_dst;
+  i64* sumsq;
+};
+
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) {
+  const i64 cpr = (a.cols + 15) / 16;
+  const i64 total = a.rows * cpr;
+  i64 sq = 0;
+  for (i64 t = (i64)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (i64)gridDim.x * blockDim.x) {
+    const i64 r = t / cpr;
+    const i64 c0 = (t - r * cpr) * 16;
+    int v[16];
+    if (VEC) {
+      const int4* p = reinterpret_cast<const int4*>(a.src + r * a.ld_src + c0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int4 x = p[q];
+        v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = (c0 + e < a.cols) ? a.src[r * a.ld_src + c0 + e] : 0;
+    }
+    i64 nud[16];
+    nudges16(a.sr, a.shift, r, c0, a.cols, nud);
+    int8_t o[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const i64 c = c0 + e;
+      const bool in = VEC || c < a.cols;
+      int x = v[e];
+      if (a.bias && in) x = add32(x, a.bias[c]);
+      const i64 mult = a.mult_col ? (in ? (i64)a.mult_col[c] : 0) : a.mult_scalar;
+      int8_t y = sat8(ams((i64)x, mult, a.shift, nud[e]));
+      if (a.relu && y < 0) y = 0;
+      if (a.mask && in && a.mask[r * a.ld_mask + c] <= 0) y = 0;
+      o[e] = in ? y : 0;
+      sq += (i64)y * y * (in ? 1 : 0);
+    }
+    if (VEC) {
+      int4 pk;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        w[q] = (uint32_t)(uint8_t)o[4 * q] | ((uint32_t)(uint8_t)o[4 * q + 1] << 8) |
+               ((uint32_t)(uint8_t)o[4 * q + 2] << 16) | ((uint32_t)(uint8_t)o[4 * q + 3] << 24);
+      *reinterpret_cast<int4*>(a.dst + r * a.ld_dst + c0) = pk;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (c0 + e < a.cols) a.dst[r * a.ld_dst + c0 + e] = o[e];
+    }
+  }
+  if (a.sumsq) block_reduce_to<false>(sq, a.sumsq);
+}
+
+struct AmsArgs {
+  const void* x;
+  int x_bits;
+  i64 rows, cols;
+  const int32_t* mult;
+  int mult_kind;
+  i64 mult_scalar;
+  int shift;
+  eco_sr_t sr;
+  i64* out;
+};
+
+__global__ void __launch_bounds__(kThreads) ams_kernel(const AmsArgs a) {
+  const i64 n = a.rows * a.cols;
+  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
+    const i64 r = i / a.cols, c = i - r * a.cols;
+    i64 x = a.x_bits == 8 ? (i64)static_cast<const int8_t*>(a.x)[i]
+            : a.x_bits == 32 ? (i64)static_cast<const int32_t*>(a.x)[i]
+                             : static_cast<const i64*>(a.x)[i];
+    const i64 m = a.mult_kind == 0 ? a.mult_scalar : (a.mult_kind == 1 ? a.mult[c] : a.mult[r]);
+    i64 nud = 0;
+    if (a.shift >= 0) {
+      if (a.sr.mode == ECO_SR_NEAREST)
+        nud = half_nudge(a.shift);
+      else if (a.sr.mode == ECO_SR_PHILOX)
+        nud = low_bits(sr_word(a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)c), a.shift);
+      else
+        nud = replay_nudge(a.sr, r, c);
+    }
+    a.out[i] = ams(x, m, a.shift, nud);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) colsum_kernel(const int8_t* g, i64 rows, i64 cols, i64 ld,
+                                                          i64* out, i64 rows_per_block) {
+  const i64 c = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const i64 r0 = (i64)blockIdx.y * rows_per_block;
+  const i64 r1 = min(rows, r0 + rows_per_block);
+  i64 s = 0;
+  for (i64 r = r0; r < r1; ++r) s += g[r * ld + c];
+  atomicAdd(reinterpret_cast<unsigned long long*>(out + c), (unsigned long long)s);
+}
+
+__global__ void __launch_bounds__(kThreads) amax_kernel(const void* x, int bits, i64 n, i64* out) {
+  i64 m = INT64_MIN;
+  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
+    i64 v;
+    if (bits == 32) {  // int32 abs wraps like torch: |INT32_MIN| stays negative
+      const int xi = static_cast<const int32_t*>(x)[i];
+      v = (i64)(int)(xi < 0 ? 0u - (unsigned)xi : (unsigned)xi);
+    } else {
+      v = abs64(static_cast<const i64*>(x)[i]);
+    }
+    m = max(m, v);
+  }
+  block_reduce_to<true>(m, out);
+}
+
+__global__ void __launch_bounds__(kThreads) sumsq_s8_kernel(const int8_t* x, i64 n, i64* out) {
+  i64 s = 0;
+  const i64 n16 = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) ? n / 16 : 0;
+  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (i64)gridDim.x * blockDim.x) {
+    const int4 q = reinterpret_cast<const int4*>(x)[i];
+    const int8_t* b = reinterpret_cast<const int8_t*>(&q);
+#pragma unroll
+    for (int e = 0; e < 16; ++e) s += (i64)b[e] * b[e];
+  }
+  for (i64 i = n16 * 16 + (i64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x)
+    s += (i64)x[i] * x[i];
+  block_reduce_to<false>(s, out);
+}
+
+__global__ void set_i64_kernel(i64* p, i64 v) { *p = v; }
+
+int grid_for(i64 work, int per_sm = 8) {
+  const i64 cap = (i64)eco_num_sms() * per_sm;
+  return (int)std::max<i64>(1, std::min<i64>(cap, (work + kThreads - 1) / kThreads));
+}
+
+}  // namespace
+
+extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols, int64_t ld_src,
+                                  const int32_t* bias_col, const int32_t* mult_col, int64_t mult_scalar,
+                                  int shift, int relu, eco_sr_t sr, const int8_t* mask, int64_t ld_mask,
+                                  int8_t* dst, int64_t ld_dst, int64_t* sumsq, eco_stream_t stream) {
+  ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && ld_src >= cols && ld_dst >= cols, ECO_ERR_ARG,
+              "eco_requant_s32_s8: bad arguments");
+  ECO_REQUIRE(!mask || ld_mask >= cols, ECO_ERR_ARG, "eco_requant_s32_s8: bad mask leading dim");
+  if (int rc = eco_check_sr(sr, shift, "eco_requant_s32_s8")) return rc;
+  cudaStream_t s = eco_stream(stream);
+  if (sumsq && cudaMemsetAsync(sumsq, 0, sizeof(int64_t), s) != cudaSuccess)
+    return eco_launch_check("eco_requant_s32_s8 memset");
+  if (rows == 0 || cols == 0) return ECO_OK;
+  RequantArgs a{src, rows, cols, ld_src, bias_col, mult_col, mult_scalar, shift, relu, sr,
+                mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq)};
+  const bool replay = sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64;
+  const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
+                   ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0)) &&
+                   (!bias_col || eco_aligned16(bias_col)) && (!mult_col || eco_aligned16(mult_col));
+  (void)replay;
+  const i64 work = rows * ((cols + 15) / 16);
+  if (vec)
+    requant_kernel<true><<<grid_for(work), kThreads, 0, s>>>(a);
+  else
+    requant_kernel<false><<<grid_for(work), kThreads, 0, s>>>(a);
+  return eco_launch_check("eco_requant_s32_s8");
+}
+
+extern "C" int eco_apply_mult_shift(const void* x, int x_bits, int64_t rows, int64_t cols,
+                                    const int32_t* mult, int mult_kind, int64_t mult_scalar, int shift,
+                                    eco_sr_t sr, int64_t* out, eco_stream_t stream) {
+  ECO_REQUIRE(x && out && rows >= 0 && cols >= 0, ECO_ERR_ARG, "eco_apply_mult_shift: bad arguments");
+  ECO_REQUIRE(x_bits == 8 || x_bits == 32 || x_bits == 64, ECO_ERR_ARG, "eco_apply_mult_shift: x_bits");
+  ECO_REQUIRE(mult_kind >= 0 && mult_kind <= 2 && (mult_kind == 0 || mult), ECO_ERR_ARG,
+              "eco_apply_mult_shift: mult_kind");
+  if (int rc = eco_check_sr(sr, shift, "eco_apply_mult_shift")) return rc;
+  if (rows * cols == 0) return ECO_OK;
+  AmsArgs a{x, x_bits, rows, cols, mult, mult_kind, mult_scalar, shift, sr, reinterpret_cast<i64*>(out)};
+  ams_kernel<<<grid_for(rows * cols), kThreads, 0, eco_stream(stream)>>>(a);
+  return eco_launch_check("eco_apply_mult_shift");
+}
+
+extern "C" int eco_colsum_s8(const int8_t* g, int64_t rows, int64_t cols, int64_t ld, int64_t* out,
+                             eco_stream_t stream) {
+  ECO_REQUIRE(g && out && rows >= 0 && cols >= 0 && ld >= cols, ECO_ERR_ARG, "eco_colsum_s8: bad arguments");
+  cudaStream_t s = eco_stream(stream);
+  if (cudaMemsetAsync(out, 0, sizeof(int64_t) * (size_t)cols, s) != cudaSuccess)
+    return eco_launch_check("eco_colsum_s8 memset");
+  if (rows == 0 || cols == 0) return ECO_OK;
+  const i64 rpb = std::max<i64>(64, (rows + 65534) / 65535);
+  dim3 grid((unsigned)((cols + kThreads - 1) / kThreads), (unsigned)((rows + rpb - 1) / rpb));
+  colsum_kernel<<<grid, kThreads, 0, s>>>(g, rows, cols, ld, reinterpret_cast<i64*>(out), rpb);
+  return eco_launch_check("eco_colsum_s8");
+}
+
+extern "C" int eco_amax(const void* x, int x_bits, int64_t n, int64_t* out, eco_stream_t stream) {
+  ECO_REQUIRE(x && out && n >= 0 && (x_bits == 32 || x_bits == 64), ECO_ERR_ARG, "eco_amax: bad arguments");
+  cudaStream_t s = eco_stream(stream);
+  // start from INT64_MIN so an all-INT_MIN input keeps torch's wrapped value
+  set_i64_kernel<<<1, 1, 0, s>>>(reinterpret_cast<i64*>(out), INT64_MIN);
+  if (n == 0) return eco_launch_check("eco_amax init");
+  amax_kernel<<<grid_for(n), kThreads, 0, s>>>(x, x_bits, n, reinterpret_cast<i64*>(out));
+  return eco_launch_check("eco_amax");
+}
+
+extern "C" int eco_sumsq_s8(const int8_t* x, int64_t n, int64_t* out, eco_stream_t stream) {
+  ECO_REQUIRE(x && out && n >= 0, ECO_ERR_ARG, "eco_sumsq_s8: bad arguments");
+  cudaStream_t s = eco_stream(stream);
+  if (cudaMemsetAsync(out, 0, sizeof(int64_t), s) != cudaSuccess) return eco_launch_check("eco_sumsq_s8 memset");
+  if (n == 0) return ECO_OK;
+  sumsq_s8_kernel<<<grid_for(n / 16 + 1), kThreads, 0, s>>>(x, n, reinterpret_cast<i64*>(out));
+  return eco_launch_check("eco_sumsq_s8");
+}

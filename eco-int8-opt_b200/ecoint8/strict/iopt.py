@@ -1,0 +1,302 @@
+"""I8ECO: integer-only ECO step (drop-in for ``ecoint8/strict/iopt.py`` v0.4.9).
+
+The reference runs ~15 eager int64 kernels per 64-row chunk with two host
+synchronisations per chunk and builds every per-row multiplier in Python.
+Here ``step()`` is ONE kernel launch for all layers (``eco_i8eco_step``): the
+per-row (mult, shift) columns of iopt.py:134-148 are derived on the device in
+IEEE double (bit-identical to Python's float arithmetic), the gradient clip
+reads the square sum that the dW requant produced, weights and momentum are
+updated in place in one pass (read w, m, g; write w, m), the momentum scale
+``s_m`` is updated on the device from the row maxima, and per-row sums of |e|
+are kept for ``stats``.  No host synchronisation.
+
+Host-visible state keeps the reference's names and types:
+``m_i8`` (int8 tensors), ``s_m`` (a list of Python floats, read from the
+device when accessed), ``step_count``, ``stats`` (``mean_abs_e`` computed from
+the row sums on first access, with the reference's summation order), ``lr``,
+``beta``, ``grad_clip``, ``chunk_rows``.  ``chunk_rows`` no longer changes the
+arithmetic; in the verification (replay) mode it orders the consumed draws
+exactly like the reference's chunk loop.
+
+Errors: where the reference raises inside ``step`` (a stochastic-rounding
+shift of 63 or more, ``torch.randint``'s ValueError), this step raises the same
+ValueError.  The bias shift is known on the host and checked before the launch
+(state untouched); a momentum / gradient shift overflow is detected by the
+kernel, which leaves that layer untouched, and is raised at the next ``step``,
+``s_m`` or ``stats`` access.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import struct
+
+import torch
+
+from .. import _native as nat
+from .. import _ops, _sr
+from ..fixedpoint import _check_int, quantize_multiplier
+
+__all__ = ["I8ECO"]
+
+FRAC_BITS = 12
+BETA_Q = 1 << 16  # beta in 16-bit fixed-point
+LR_Q = 1 << 16  # lr in 16-bit fixed-point (requires lr < 2)
+
+
+def _bits(v: float) -> int:
+    return struct.unpack("<q", struct.pack("<d", float(v)))[0]
+
+
+def _float(b: int) -> float:
+    return struct.unpack("<d", struct.pack("<q", int(b)))[0]
+
+
+def _col_mults(ratios: list[float], dev: torch.device) -> tuple[torch.Tensor, int]:
+    """Per-row ``(mult, shift)`` pairs sharing one common shift (iopt.py:42-54)."""
+    ms = [quantize_multiplier(r) for r in ratios]
+    com = min(s for _, s in ms)
+    mults = torch.tensor([m >> (s - com) for m, s in ms], dtype=torch.int32, device=dev)
+    return mults.unsqueeze(1), com
+
+
+def _common_shift(ratios) -> int:
+    return min(quantize_multiplier(r)[1] for r in ratios)
+
+
+class _ScaleView(list):
+    """``s_m`` as a list of floats; item assignment writes through to the optimizer."""
+
+    def __init__(self, opt, values):
+        super().__init__(values)
+        self._opt = opt
+
+    def __setitem__(self, i, v):
+        super().__setitem__(i, v)
+        self._opt.s_m = list(self)
+
+
+class I8ECO:
+    """Fully integer ECO-SGDM for ``I8Linear`` layers.  Zero fp32 state or temporaries."""
+
+    def __init__(self, layers, lr: float = 0.5, momentum: float = 0.9, grad_clip: float | None = 1.0,
+                 chunk_rows: int = 64):
+        assert momentum > 0, "ECO requires beta > 0"
+        assert 0.0 < lr < 2.0, "lr must fit 16-bit fixed-point (0, 2)"
+        assert chunk_rows >= 1, "chunk_rows must be positive"
+        self.layers = list(layers)
+        self.lr = float(lr)
+        self.beta = float(momentum)
+        self.grad_clip = grad_clip
+        self.chunk_rows = int(chunk_rows)
+        self.m_i8 = [torch.zeros_like(layer.w_i8) for layer in self.layers]
+        self._s_m_host = [1.0 for _ in self.layers]
+        self._state = None  # device int64 [L, 4]: s_m bits, row-max accumulator, error flags, spare
+        self._counter = None
+        self._rowsum: list[torch.Tensor | None] = [None] * len(self.layers)
+        self._pending_stats = None
+        self._err = None  # (event, pinned flags) of the last launch
+        self.step_count = 0
+        self._stats = {"skipped": 0, "mean_abs_e": 0.0}
+
+    # -- reference attributes ----------------------------------------------
+    @property
+    def s_m(self) -> list[float]:
+        if self._state is None:
+            return _ScaleView(self, self._s_m_host)
+        self._raise_pending(block=True)
+        return _ScaleView(self, [_float(b) for b in self._state[:, 0].tolist()])
+
+    @s_m.setter
+    def s_m(self, values) -> None:
+        values = [float(v) for v in values]
+        assert len(values) == len(self.layers)
+        if self._state is None:
+            self._s_m_host = values
+        else:
+            self._state[:, 0].copy_(torch.tensor([_bits(v) for v in values], dtype=torch.int64))
+
+    @property
+    def stats(self) -> dict:
+        if self._pending_stats is not None:
+            self._raise_pending(block=True)
+            tot_e, n_e = 0.0, 0
+            for rowsum, sw, rowlen, out in self._pending_stats:
+                rs = rowsum.tolist()
+                tot_e += sum(s * sw_o for s, sw_o in zip(rs, sw)) / rowlen / (1 << FRAC_BITS)  # iopt.py:183
+                n_e += out
+            if n_e:
+                self._stats["mean_abs_e"] = tot_e / n_e
+            self._pending_stats = None
+        return self._stats
+
+    @stats.setter
+    def stats(self, value: dict) -> None:
+        self._pending_stats = None
+        self._stats = value
+
+    def set_lr(self, lr: float):
+        assert 0.0 < lr < 2.0, "lr must fit 16-bit fixed-point (0, 2)"
+        self.lr = float(lr)
+
+    # -- device state ------------------------------------------------------
+    def _ensure_state(self, dev: torch.device) -> None:
+        if self._state is not None and self._state.device == dev:
+            return
+        s_m = self._s_m_host if self._state is None else self.s_m
+        st = torch.zeros((len(self.layers), 4), dtype=torch.int64)
+        st[:, 0] = torch.tensor([_bits(v) for v in s_m], dtype=torch.int64)
+        self._state = st.to(dev)
+        self._counter = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def _raise_pending(self, block: bool) -> None:
+        if self._err is None:
+            return
+        event, flags = self._err
+        if not block and not event.query():
+            return
+        event.synchronize()
+        self._err = None
+        bad = [(i, int(f)) for i, f in enumerate(flags.tolist()) if f]
+        if bad:
+            self._state[:, 2].zero_()
+            i, f = bad[0]
+            if f & nat.FLAG_SHIFT_OVERFLOW:
+                # the reference raises here from torch.randint(0, 2**shift) with shift >= 63
+                raise ValueError(f"Overflow when unpacking long long (I8ECO layer {i}: a requant shift "
+                                 "exceeded 62; that layer was left unchanged)")
+            raise ValueError(f"I8ECO layer {i}: invalid scale ratio (flags {f}); layer left unchanged")
+
+    def _gsq(self, layer, g: torch.Tensor) -> torch.Tensor:
+        """sum g^2 on the device: the dW requant's by-product, or one reduction."""
+        if getattr(layer, "_gw_sumsq_of", None) is g and getattr(layer, "_gw_sumsq", None) is not None:
+            return layer._gw_sumsq
+        return _ops.sumsq(g)
+
+    # -- step ------------------------------------------------------------
+    @torch.no_grad()
+    def step(self):
+        self._raise_pending(block=False)
+        b = self.beta
+        alpha = (1.0 / self.lr) * (1.0 - 1.0 / b)
+        b_q = round(b * BETA_Q)
+        nb_q = round((1.0 - b) * BETA_Q)
+        lr_q = round(self.lr * LR_Q)
+        a_q = round(alpha * BETA_Q)
+        self.step_count += 1
+        F = FRAC_BITS
+        active = [(i, layer) for i, layer in enumerate(self.layers) if layer._gw_i8 is not None]
+        if not active:
+            return
+        dev = nat.require_cuda(*[layer.w_i8 for _, layer in active])
+        self._ensure_state(dev)
+        replay = _sr.replaying()
+        if replay:
+            s_m_now = [_float(v) for v in self._state[:, 0].tolist()]
+        keep = []  # tensors that must outlive the launch
+        descs = []
+        pending = []
+        for i, layer in active:
+            g_i8 = layer._gw_i8
+            _check_int(g_i8, "weight grad")
+            w = layer.w_i8
+            if self.m_i8[i].device != w.device:  # layer moved after construction: follow it
+                self.m_i8[i] = self.m_i8[i].to(w.device)
+            m = self.m_i8[i]
+            nat.require_cuda(g_i8, w, m)
+            g = g_i8.contiguous()
+            if g.dtype != torch.int8 or not (w.is_contiguous() and m.is_contiguous()) or g.shape != w.shape:
+                raise RuntimeError("I8ECO: weights, momentum and gradient must be contiguous int8 of one shape")
+            out, rowlen = g.shape
+            s_g = float(layer._gw_s)
+            sw_bits, sw_min, sw_max = layer._sw_device(dev)
+            gsq = self._gsq(layer, g) if self.grad_clip is not None else None
+            if self._rowsum[i] is None or self._rowsum[i].numel() != out or self._rowsum[i].device != dev:
+                self._rowsum[i] = torch.empty(out, dtype=torch.int64, device=dev)
+            d = nat.I8ECOLayer()
+            d.w, d.m, d.g, d.sw = w.data_ptr(), m.data_ptr(), g.data_ptr(), sw_bits.data_ptr()
+            d.rowsum, d.gsq = self._rowsum[i].data_ptr(), nat.ptr(gsq)
+            d.state = self._state[i].data_ptr()
+            d.rows, d.cols = out, rowlen
+            d.sw_min, d.sw_max, d.s_g = sw_min, sw_max, s_g
+            d.stream_w, d.stream_b = 2 * i, 2 * i + 1
+            d.nudge_m_bits = d.nudge_b_bits = 32
+            if layer.use_bias:
+                assert isinstance(layer.sx, float)
+                gb = layer._gb_sum.to(device=dev, dtype=torch.int64).contiguous()
+                s_gb = float(layer._gb_s)
+                com_b = _common_shift([self.lr * s_gb / (layer.sx * sw_min)])  # = min over rows
+                if com_b > 62:  # the reference's torch.randint(0, 2**com_b) raises (iopt.py:194)
+                    raise ValueError("Overflow when unpacking long long")
+                d.b_acc, d.gb_sum, d.s_gb, d.sx = layer.b_acc.data_ptr(), gb.data_ptr(), s_gb, layer.sx
+                keep.append(gb)
+            if replay:
+                keep += self._replay_nudges(d, layer, s_m_now[i], s_g, gsq, g.shape)
+            keep += [g, gsq, sw_bits]
+            descs.append(d)
+            pending.append((self._rowsum[i], list(layer.sw), rowlen, out))
+        hyper = nat.I8ECOHyper()
+        hyper.lr = self.lr
+        hyper.grad_clip = -1.0 if self.grad_clip is None else float(self.grad_clip)
+        hyper.b_q, hyper.nb_q, hyper.lr_q, hyper.a_q = b_q, nb_q, lr_q, a_q
+        hyper.sr_mode = nat.SR_REPLAY32 if replay else nat.SR_PHILOX
+        hyper.seed = 0 if replay else _sr.new_key()
+        hyper.done_counter = self._counter.data_ptr()
+        if _sr.LOG is not None and not replay:
+            _sr.LOG.append(("i8eco_step", hyper.seed, [(i, 2 * i, 2 * i + 1) for i, _ in active]))
+        arr = (nat.I8ECOLayer * len(descs))(*descs)
+        nat.call("eco_i8eco_step", arr, len(descs), ctypes.byref(hyper), nat.stream())
+        self._pending_stats = pending
+        flags = torch.empty(len(self.layers), dtype=torch.int64, pin_memory=True)
+        flags.copy_(self._state[:, 2], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._err = (ev, flags)
+        self._keep = keep  # released at the next step (stream-ordered reuse is safe)
+
+    def _replay_nudges(self, d, layer, s_m: float, s_g: float, gsq, shape):
+        """Verification mode: draw in the reference's order (iopt.py:152-197), consume whole.
+
+        Host scalars follow the reference expressions; the kernel recomputes the
+        same shifts on the device.
+        """
+        F = FRAC_BITS
+        out, rowlen = shape
+        dev = layer.w_i8.device
+        if self.grad_clip is not None:
+            sq_sum = int(gsq.item())
+            n_real = math.sqrt(sq_sum) * s_g
+            if n_real > self.grad_clip:
+                s_g = s_g * (self.grad_clip / n_real)
+        com_mm = _common_shift([(sw_o / (1 << F)) / s_m if s_m > 0 else 0.0 for sw_o in layer.sw])
+        ws, ms = [], []
+        for c in range(0, out, self.chunk_rows):
+            rows = min(c + self.chunk_rows, out) - c
+            ws.append(_sr.replay_draw((rows, rowlen), 1 << F, dev).to(torch.int32))
+            if com_mm >= 0:
+                ms.append(_sr.replay_draw((rows, rowlen), 1 << com_mm, dev))
+        nw = torch.cat(ws).contiguous()
+        nm = torch.cat(ms).contiguous() if ms else torch.zeros(1, dtype=torch.int32, device=dev)
+        d.nudge_w, d.nudge_m = nw.data_ptr(), nm.data_ptr()
+        d.nudge_m_bits = 64 if nm.dtype == torch.int64 else 32
+        kept = [nw, nm]
+        if layer.use_bias:
+            com_b = _common_shift([self.lr * float(layer._gb_s) / (layer.sx * sw_o) for sw_o in layer.sw])
+            if com_b >= 0:
+                nb = _sr.replay_draw((out, 1), 1 << com_b, dev).reshape(out).contiguous()
+            else:
+                nb = torch.zeros(1, dtype=torch.int32, device=dev)
+            d.nudge_b = nb.data_ptr()
+            d.nudge_b_bits = 64 if nb.dtype == torch.int64 else 32
+            kept.append(nb)
+        return kept
+
+    @torch.no_grad()
+    def zero_grad(self):
+        for layer in self.layers:
+            layer._gw_i8 = None
+
+    def memory_bytes(self) -> int:
+        """Stored integer state in bytes (int8 weights live on layers; int8 momentum here)."""
+        return sum(m.numel() for m in self.m_i8)

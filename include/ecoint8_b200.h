@@ -1,0 +1,188 @@
+/*
+ * ecoint8_b200.h — C ABI of the B200 (sm_100a) library behind the ecoint8
+ * strict int8 training path.
+ *
+ * Every entry point takes plain device pointers, sizes and a stream, returns
+ * an int status (ECO_OK or a negative ECO_ERR_*), never synchronises the
+ * host, and never allocates device memory: outputs, scratch words and
+ * optimizer state are owned by the caller.  Work is enqueued on `stream`
+ * (a cudaStream_t; NULL = the legacy default stream).  After a failure,
+ * eco_last_error() returns a message for the calling thread.
+ *
+ * Matrices are row-major with an explicit leading dimension in elements.
+ * Stochastic rounding (SR) draws follow the caller's eco_sr_t:
+ *   ECO_SR_NEAREST  round half up: nudge = 2^(shift-1)      (fixedpoint.py:72-73)
+ *   ECO_SR_PHILOX   nudge = low `shift` bits of the library's Philox4x32-10
+ *                   word for (seed, stream, row_base + row, col)
+ *   ECO_SR_REPLAY32 / ECO_SR_REPLAY64
+ *                   nudge[row * nudge_ld + col], an int32 / int64 tensor such
+ *                   as the reference's own torch.randint draw (fixedpoint.py:40-49)
+ * Citations name files of the reference package ecoint8 v0.4.9.
+ */
+#ifndef ECOINT8_B200_H
+#define ECOINT8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ECO_API __attribute__((visibility("default")))
+#else
+#define ECO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ECO_ABI_VERSION 1
+
+enum {
+  ECO_OK = 0,
+  ECO_ERR_ARG = -1,         /* bad pointer / size / layout argument */
+  ECO_ERR_MISALIGNED = -2,  /* a TMA operand is not 16-byte aligned (address or leading dim) */
+  ECO_ERR_ARCH = -3,        /* device is not sm_100 */
+  ECO_ERR_LAUNCH = -4,      /* CUDA launch / driver error */
+  ECO_ERR_RANGE = -5,       /* a requant shift outside [-63, 62] */
+};
+
+enum { ECO_SR_NEAREST = 0, ECO_SR_PHILOX = 1, ECO_SR_REPLAY32 = 2, ECO_SR_REPLAY64 = 3 };
+
+typedef void* eco_stream_t; /* cudaStream_t */
+
+typedef struct {
+  int32_t mode;        /* ECO_SR_* */
+  int32_t pad_;
+  const void* nudge;   /* replay modes: [rows, nudge_ld] int32 or int64 */
+  int64_t nudge_ld;
+  uint64_t seed;       /* Philox key */
+  uint64_t stream;     /* Philox site id (unique per draw site) */
+  int64_t row_base;    /* global row index of local row 0 (data parallel shards) */
+} eco_sr_t;
+
+ECO_API int eco_abi_version(void);
+ECO_API const char* eco_last_error(void);
+/* 1 when `device` is an sm_100 (B200-class) GPU, 0 otherwise, <0 on error. */
+ECO_API int eco_device_supported(int device);
+
+/* ---------------------------------------------------------------- GEMMs --
+ * C[M,N] = A[M,K] . B[K,N] on int8 tcgen05 tensor cores, int32 accumulate.
+ * a_layout 0: A stored [M, lda] (K contiguous);  1: A stored [K, lda] (M contiguous)
+ * b_layout 0: B stored [N, ldb] (K contiguous);  1: B stored [K, ldb] (N contiguous)
+ * Operands need 16-byte aligned base addresses and leading dims (ECO_ERR_MISALIGNED).
+ */
+
+/* C = A.B (+ bias[n], int32 wrap-around; bias nullable).  `amax` (nullable,
+ * device int32) is overwritten with max |C|.
+ * Replaces torch._int_mm at ecoint8/strict/ilayer.py:40-54 (called from :117,
+ * :135, :152, :159), the `acc + b_acc` of :118-119 and the int_amax reductions
+ * at :121, :153, :161. */
+ECO_API int eco_gemm_s8s32(const int8_t* A, int64_t lda, int a_layout, const int8_t* B, int64_t ldb,
+                   int b_layout, int64_t M, int64_t N, int64_t K, const int32_t* bias, int32_t* C,
+                   int64_t ldc, int32_t* amax, eco_stream_t stream);
+
+/* Y = sat8(relu?( SR((C + bias[n]) * mult[n], shift) )) fused in the GEMM epilogue.
+ * Replaces ilayer.py:135-141 (_int_mm + b_acc + _common_shift_requant :57-70) and,
+ * with relu=1, the I8ReLU.apply_forward clamp that follows (:180-182). */
+ECO_API int eco_gemm_s8_requant(const int8_t* A, int64_t lda, int a_layout, const int8_t* B, int64_t ldb,
+                        int b_layout, int64_t M, int64_t N, int64_t K, const int32_t* bias,
+                        const int32_t* mult, int shift, int relu, eco_sr_t sr, int8_t* Y,
+                        int64_t ldy, eco_stream_t stream);
+
+/* ---------------------------------------------------------- elementwise --
+ * dst = sat8(SR((src + bias[c]) * m, shift)), m = mult_col[c] or mult_scalar;
+ * then dst = 0 where mask[r,c] <= 0 (mask nullable); relu clamps at 0;
+ * sumsq (nullable, device int64) is overwritten with sum(dst^2).
+ * Replaces the dX / dW requant of ilayer.py:155, :163, the relu mask of
+ * :184-188 and the grad-clip square sum of iopt.py:96. */
+ECO_API int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols, int64_t ld_src,
+                       const int32_t* bias_col, const int32_t* mult_col, int64_t mult_scalar,
+                       int shift, int relu, eco_sr_t sr, const int8_t* mask, int64_t ld_mask,
+                       int8_t* dst, int64_t ld_dst, int64_t* sumsq, eco_stream_t stream);
+
+/* out = apply_mult_shift(x, mult, shift) as int64, no saturation.
+ * x_bits 8/32/64; mult_kind 0 scalar, 1 per column [cols], 2 per row [rows].
+ * Replaces fixedpoint.apply_mult_shift (fixedpoint.py:52-76) on CUDA tensors. */
+ECO_API int eco_apply_mult_shift(const void* x, int x_bits, int64_t rows, int64_t cols, const int32_t* mult,
+                         int mult_kind, int64_t mult_scalar, int shift, eco_sr_t sr, int64_t* out,
+                         eco_stream_t stream);
+
+/* out[c] = sum_r g[r, c] (int64).  Replaces ilayer.py:168 (g.int32.sum(0)). */
+ECO_API int eco_colsum_s8(const int8_t* g, int64_t rows, int64_t cols, int64_t ld, int64_t* out,
+                  eco_stream_t stream);
+
+/* *out = max |x| over n int32/int64 elements (device int64 word, overwritten).
+ * Replaces fixedpoint.int_amax's reduction (fixedpoint.py:85-88). */
+ECO_API int eco_amax(const void* x, int x_bits, int64_t n, int64_t* out, eco_stream_t stream);
+
+/* *out = sum x^2 over n int8 elements (device int64, overwritten).  iopt.py:96. */
+ECO_API int eco_sumsq_s8(const int8_t* x, int64_t n, int64_t* out, eco_stream_t stream);
+
+/* Reads and clears the sticky device error flags (bit 4: a bounded device wait
+ * gave up).  Synchronises the device.  No reference counterpart: the reference
+ * has no device-side waits. */
+ECO_API int eco_read_device_errors(uint32_t* flags);
+
+/* 2-D strided int8 copy (relayout to a 16-byte aligned leading dimension). */
+ECO_API int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_t ld_dst, int64_t rows,
+                  int64_t cols, eco_stream_t stream);
+
+/* -------------------------------------------------------- I8ECO step -----
+ * One fused, single-pass integer ECO-SGDM step over a list of layers
+ * (ecoint8/strict/iopt.py:103-200): per-row fixed-point multipliers and common
+ * shifts are derived on the device from the scales (iopt.py:134-148), grad clip
+ * from the device square sum (:90-101), weights and momentum are updated in
+ * place, the momentum scale s_m is updated on the device from the row maxima
+ * (:178-180), per-row sums of |e| are written for the statistics (:183), and
+ * the bias takes its integer SGD step (:187-197).  No host synchronisation.
+ */
+typedef struct {
+  int8_t* w;              /* [rows, cols] contiguous, updated in place */
+  int8_t* m;              /* [rows, cols] contiguous momentum, updated in place */
+  const int8_t* g;        /* [rows, cols] contiguous int8 weight gradient */
+  const double* sw;       /* [rows] frozen per-row weight steps */
+  int64_t* rowsum;        /* [rows] out: sum_j |e| (nullable) */
+  const int64_t* gsq;     /* device sum g^2 (required when grad clipping) */
+  int64_t* state;         /* device int64[4]: [0] s_m (double bits), [1] row-max
+                             accumulator (double bits, zero between steps), [2] error flags */
+  int32_t* b_acc;         /* [rows] int32 bias accumulator (nullable: no bias) */
+  const int64_t* gb_sum;  /* [rows] int64 bias gradient column sums */
+  const void* nudge_w;    /* replay: [rows, cols] int32 weight nudges */
+  const void* nudge_m;    /* replay: [rows, cols] int32/int64 momentum nudges */
+  const void* nudge_b;    /* replay: [rows] int32/int64 bias nudges */
+  int64_t rows, cols;
+  double sw_min, sw_max;  /* min / max of sw */
+  double s_g;             /* layer._gw_s */
+  double s_gb, sx;        /* layer._gb_s, layer.sx (bias step) */
+  uint64_t stream_w;      /* Philox site of the weight / momentum nudges */
+  uint64_t stream_b;      /* Philox site of the bias nudges */
+  int32_t nudge_m_bits;   /* 32 or 64 */
+  int32_t nudge_b_bits;   /* 32 or 64 */
+} eco_i8eco_layer_t;
+
+typedef struct {
+  double lr;
+  double grad_clip;     /* < 0: no clipping (grad_clip=None) */
+  int64_t b_q, nb_q, lr_q, a_q; /* iopt.py:107-110 */
+  int32_t sr_mode;      /* ECO_SR_PHILOX or a replay mode (replay uses the layer nudges) */
+  int32_t pad_;
+  uint64_t seed;
+  uint32_t* done_counter; /* device word, zero between steps (reset by the kernel) */
+} eco_i8eco_hyper_t;
+
+ECO_API int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, const eco_i8eco_hyper_t* hyper,
+                   eco_stream_t stream);
+
+/* --------------------------------------------------- EcoInt8SGDM step -----
+ * The fused fp32-transient ECO step of EcoInt8SGDM (ecoint8/eco.py:330-362),
+ * replacing the Triton kernels and their host glue (triton_kernels.py:127-170):
+ * max|g|, pass 1 (max |m_new|), pass 2 (store w and m), sm <- sm_new.  `scratch`
+ * is a device buffer of 4 uint32 words (cleared by the call). */
+ECO_API int eco_sgdm_step(int8_t* w, int8_t* m, const float* g, int64_t rows, int64_t cols,
+                  const float* sw, float* sm, float lr, float beta, float wd, float alpha,
+                  uint64_t seed, uint32_t* scratch, eco_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ECOINT8_B200_H */

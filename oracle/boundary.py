@@ -3,7 +3,7 @@
 The strict region is entered and left through fp32 code the reference keeps in
 ``ecoint8/quant.py`` (entry quantization, ``quantize_tensor_dynamic`` on the
 loss gradient).  These are restated with torch CPU ops so that they consume the
-global torch generator exactly as the reference does (``quant.py:10-38``).
+global torch generator exactly as the reference does (``quant.py:9-38``).
 
 The seeded workloads (the 32-64-2 blob task, the 784-256-128-10 MNIST-shaped
 task) are defined here once, so the golden generator, the oracle tests and the
@@ -18,7 +18,7 @@ EPS = 1e-8  # quant.py:7
 
 
 def calc_scale(amax: float, clip=None) -> float:
-    """quant.py:10-17."""
+    """quant.py:9-16."""
     a = float(amax)
     if clip is not None:
         a = min(a, clip)
@@ -28,7 +28,7 @@ def calc_scale(amax: float, clip=None) -> float:
 
 
 def quantize_symmetric(x, scale, stochastic=False):
-    """quant.py:20-29 (torch CPU or CUDA tensors; uses the global generator)."""
+    """quant.py:19-28 (torch CPU or CUDA tensors; uses the global generator)."""
     import torch
 
     s = scale + EPS
@@ -41,7 +41,7 @@ def quantize_symmetric(x, scale, stochastic=False):
 
 
 def quantize_tensor_dynamic(x, stochastic=False):
-    """quant.py:36-39."""
+    """quant.py:35-38."""
     amax = x.detach().abs().max().item()
     return quantize_symmetric(x, calc_scale(amax), stochastic), calc_scale(amax)
 

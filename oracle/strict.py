@@ -282,13 +282,17 @@ class I8ECO:
         mmm, cmm = col_mults([(sw_o / (1 << F)) / s_m if s_m > 0 else 0.0 for sw_o in sw])
         return (mm[:, None], cm), (mg[:, None], cg), (mmm[:, None], cmm)
 
-    def step(self, draw=None, nudges=None):
+    def step(self, draw=None, nudges=None, philox=None):
         """iopt.py:103-200.
 
-        Either ``draw`` (consumed in the reference's chunk order) or ``nudges``: a
+        Either ``draw`` (consumed in the reference's chunk order), ``nudges``: a
         list with one ``(nudge_w [out,in], nudge_m [out,in] | None, nudge_b
-        [out,1] | None)`` per layer, consumed whole (the CUDA single-pass order).
+        [out,1] | None)`` per layer, consumed whole (the CUDA single-pass order),
+        or ``philox=(seed, {layer: (stream_w, stream_b)})``: the CUDA library's
+        Philox stream (``oracle/philox.py:step_nudges``).
         """
+        if philox is not None:
+            nudges = self._philox_nudges(*philox)
         F = FRAC_BITS
         b_q, nb_q, lr_q, a_q = fixed_point_consts(self.lr, self.beta)
         self.step_count += 1
@@ -345,6 +349,30 @@ class I8ECO:
                                    - delta[:, 0].astype(np.int32).astype(np.int64)).astype(np.int32)
         if n_e:
             self.stats["mean_abs_e"] = tot_e / n_e
+
+    def _philox_nudges(self, seed, streams):
+        """Whole-layer nudges of the Philox stream, with this step's shifts."""
+        from . import philox as ph
+
+        res = []
+        for i, layer in enumerate(self.layers):
+            if layer._gw_i8 is None or i not in streams:
+                res.append(None)
+                continue
+            s_g = float(layer._gw_s)
+            _, s_g = self.clip_grad(layer._gw_i8, s_g)
+            (_, _), (_, _), (_, cmm) = self.layer_mults(i, s_g)
+            out, cols = layer._gw_i8.shape
+            sw_, sb_ = streams[i]
+            nw, nm = ph.step_nudges(seed, sw_, out, cols, cmm)
+            nb = None
+            if layer.use_bias:
+                _, cb = col_mults([self.lr * float(layer._gb_s) / (layer.sx * sw_o) for sw_o in layer.sw])
+                if cb >= 0:
+                    r = np.arange(out, dtype=np.uint64)[:, None]
+                    nb = ph.low_bits(ph.sr_word(seed, sb_, r, np.zeros_like(r)), cb)
+            res.append((nw, nm, nb))
+        return res
 
     def zero_grad(self):
         for layer in self.layers:

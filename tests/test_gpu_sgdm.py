@@ -1,0 +1,78 @@
+"""EcoInt8SGDM's fused CUDA step against the oracle restatement of the Triton kernels.
+
+The oracle (oracle/sgdm.py) is pinned to the reference's Triton kernels run by
+Triton's interpreter (tests/test_oracle_golden.py).  The CUDA step follows the
+reference as it runs on a GPU, where PyTorch divides a CUDA tensor by a
+Python scalar as a multiply by the fp32 reciprocal; the oracle's
+``division="cuda"`` mode models exactly that, and the first test checks the
+model against PyTorch on this device.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sgdm as osg
+
+pytestmark = pytest.mark.gpu
+
+
+def test_torch_cuda_divides_by_scalar_via_reciprocal():
+    x = torch.rand(1 << 16, generator=torch.Generator().manual_seed(1)) * 3.0
+    got = (x.cuda() / 127.0).cpu().numpy()
+    ref = (x.numpy() * np.float32(np.float32(1.0) / np.float32(127.0))).astype(np.float32)
+    assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("rows,cols,wd,seed", [(8, 300, 0.0, 1234), (5, 1000, 0.01, 77), (33, 64, 0.0, 5),
+                                               (512, 1024, 0.0, 2 ** 31 - 1), (3, 7, 0.1, 0)])
+def test_fused_step_equals_oracle(rows, cols, wd, seed):
+    from ecoint8.triton_kernels import triton_eco_step_
+
+    gen = torch.Generator().manual_seed(rows * cols)
+    w = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, generator=gen)
+    m = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, generator=gen)
+    g = torch.randn(rows, cols, generator=gen) * 1e-2
+    sw = torch.rand(rows, generator=gen) * 0.01 + 1e-3
+    sm = torch.tensor(0.05, dtype=torch.float32)
+    ref = osg.triton_step(w.numpy(), m.numpy(), g.numpy(), sw.numpy(), sm.numpy(), lr=0.5, beta=0.9, wd=wd,
+                          seed=seed, division="cuda")
+    wc, mc, smc = w.cuda(), m.cuda(), sm.clone().cuda()
+    scratch = torch.empty(8192, dtype=torch.float32, device="cuda")
+    assert triton_eco_step_(wc, mc, g.cuda(), sw.cuda(), smc, lr=0.5, beta=0.9, wd=wd, seed=seed,
+                            scratch=scratch) == "ok"
+    assert np.array_equal(wc.cpu().numpy(), ref["w"])
+    assert np.array_equal(mc.cpu().numpy(), ref["m"])
+    assert smc.cpu().numpy().view(np.int32) == ref["sm_new"].view(np.int32)
+
+
+def test_optimizer_trains_int8linear_net():
+    """EcoInt8SGDM on Int8Linear layers (tests/test_triton.py:57-82 task): learns, fused every step."""
+    import torch.nn as nn
+
+    from ecoint8 import EcoInt8SGDM, Int8Linear
+
+    torch.manual_seed(0)
+    X = torch.randn(512, 20).cuda()
+    y = ((X[:, :5].sum(1)) > 0).long()
+
+    class N(nn.Module):
+        def __init__(s):
+            super().__init__()
+            s.fc1 = Int8Linear(20, 32)
+            s.fc2 = Int8Linear(32, 2)
+
+        def forward(s, x):
+            return s.fc2(torch.relu(s.fc1(x)))
+
+    net = N().cuda()
+    opt = EcoInt8SGDM([net.fc1, net.fc2], lr=0.5, momentum=0.9)
+    fn = nn.CrossEntropyLoss()
+    for _ in range(60):
+        loss = fn(net(X), y)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+    acc = (net(X).argmax(1) == y).float().mean().item()
+    assert opt.last_step_backend == "cuda" and opt.stats["fused_steps"] == 120
+    assert acc > 0.8, acc

@@ -1,0 +1,158 @@
+"""Host-side checks that need no GPU: the C ABI library, the drop-in surface, host logic."""
+
+import pathlib
+import re
+
+import pytest
+import torch
+
+REPO = pathlib.Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "ecoint8_b200.h"
+PKG = REPO / "eco-int8-opt_b200" / "ecoint8"
+
+
+def _header_functions():
+    return re.findall(r"^ECO_API\s+[\w\s\*]+?\b(eco_\w+)\s*\(", HEADER.read_text(), flags=re.M)
+
+
+def test_library_loads_and_exports_every_header_symbol():
+    from ecoint8 import _native
+
+    lib = _native.load()
+    names = _header_functions()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(lib, n), n
+    assert sorted(names) == sorted(_native.exported_symbols())
+    assert lib.eco_abi_version() == 1
+
+
+def test_c_abi_rejects_bad_arguments_with_a_message():
+    """Argument errors come back as status codes with eco_last_error(), no device work."""
+    from ecoint8 import _native
+
+    lib = _native.load()
+    rc = lib.eco_colsum_s8(None, 4, 4, 4, None, None)
+    assert rc == -1 and "bad arguments" in _native.last_error()
+    spec = _native.sr_spec(_native.SR_REPLAY32)
+    rc = lib.eco_requant_s32_s8(1, 1, 1, 1, None, None, 1, 5, 0, spec, None, 0, 1, 1, None, None)
+    assert rc == -1 and "nudge" in _native.last_error()
+    spec = _native.sr_spec(_native.SR_NEAREST)
+    rc = lib.eco_requant_s32_s8(1, 1, 1, 1, None, None, 1, 63, 0, spec, None, 0, 1, 1, None, None)
+    assert rc == -5 and "62" in _native.last_error()
+    rc = lib.eco_gemm_s8s32(16, 10, 0, 32, 16, 0, 4, 4, 4, None, 64, 4, None, None)
+    assert rc == -2 and "aligned" in _native.last_error()
+
+
+def test_no_cpu_path_fails_loudly():
+    from ecoint8 import I8Linear, I8ECO
+    from ecoint8 import fixedpoint as fp
+
+    torch.manual_seed(0)
+    lin = I8Linear(32, 16)
+    lin.sx, lin.sy = 0.01, 0.05
+    with pytest.raises(RuntimeError, match="CUDA"):
+        lin.forward_i8(torch.zeros(4, 32, dtype=torch.int8))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fp.apply_mult_shift(torch.ones(3, dtype=torch.int32), 3, 2)
+    lin._gw_i8 = torch.zeros(16, 32, dtype=torch.int8)
+    lin._gw_s = 1e-3
+    with pytest.raises(RuntimeError, match="CUDA"):
+        I8ECO([lin]).step()
+
+
+STRICT = ["fixedpoint.py", "strict/ilayer.py", "strict/iopt.py"]
+BANNED = [".float(", "torch.float32", "torch.float(", "to(torch.float", ".double("]
+
+
+def test_no_float_ops_in_strict_sources():
+    """The reference's static audit (tests/test_strict.py:17-32) on the drop-in's sources."""
+    for name in STRICT:
+        src = (PKG / name).read_text()
+        for pat in BANNED:
+            assert pat not in src, f"{name} contains banned {pat!r}"
+
+
+def test_public_api_matches_reference_surface():
+    import ecoint8
+    from ecoint8 import fixedpoint, quant
+    from ecoint8.strict import I8ECO, I8Linear, I8ReLU, I8Sequential  # noqa: F401
+    from ecoint8.triton_kernels import TRITON_AVAILABLE, triton_eco_step_  # noqa: F401
+
+    for name in ["EcoInt8SGDM", "EcoSGDM", "EcoAdam", "I8ECO", "I8Linear", "I8ReLU", "I8Sequential", "Int8Linear",
+                 "to_int8", "quantize_symmetric", "quantize_tensor_dynamic", "quantize_per_channel", "dequantize"]:
+        assert hasattr(ecoint8, name), name
+    assert ecoint8.__version__ == "0.4.9"
+    for name in ["quantize_multiplier", "apply_mult_shift", "to_int8_sat", "int_amax", "pad_mm_dims",
+                 "dynamic_scale_from_int", "_check_int", "_sr_nudge"]:
+        assert hasattr(fixedpoint, name), name
+    for name in ["calc_scale", "quantize_symmetric", "quantize_tensor_dynamic", "quantize_per_channel",
+                 "dequantize", "saturation_ratio"]:
+        assert hasattr(quant, name), name
+    with pytest.raises(NotImplementedError):
+        ecoint8.EcoSGDM([])
+
+
+def test_scalar_bookkeeping_is_the_reference_arithmetic():
+    """quantize_multiplier / pad_mm_dims / dynamic_scale_from_int equal the oracle's (pinned) ones."""
+    from ecoint8 import fixedpoint as fp
+    from oracle import fixedpoint as ofp
+
+    gen = torch.Generator().manual_seed(0)
+    rs = torch.exp(torch.empty(5000, dtype=torch.float64).uniform_(-60, 20, generator=gen)).tolist()
+    for r in rs + [0.0, 1.0, 0.5, 1 - 2 ** -40]:
+        assert fp.quantize_multiplier(r) == ofp.quantize_multiplier(r)
+    for m, k, n in [(1, 1, 1), (17, 13, 5), (4097, 4097, 1000)]:
+        assert fp.pad_mm_dims(m, k, n) == ofp.pad_mm_dims(m, k, n)
+    assert fp.dynamic_scale_from_int(0, 3.0) == 1.0
+
+
+def test_state_is_integral_and_scales_are_floats():
+    """tests/test_strict.py:45-56 minus the device work: buffers integral, s_m floats."""
+    from ecoint8 import I8ECO, I8Linear, I8ReLU, I8Sequential
+
+    net = I8Sequential(I8Linear(20, 32), I8ReLU(), I8Linear(32, 2))
+    opt = I8ECO(net.int8_layers(), lr=0.5, momentum=0.9)
+    for t, p in net.named_buffers():
+        assert p.dtype in {torch.int8, torch.int32, torch.int64}, t
+    assert all(m.dtype == torch.int8 for m in opt.m_i8)
+    assert all(isinstance(s, float) for s in opt.s_m)
+    opt.s_m[1] = 0.25
+    assert opt.s_m == [1.0, 0.25]
+    assert opt.memory_bytes() == 20 * 32 + 32 * 2
+
+
+def test_weight_steps_track_edits_and_pickle():
+    import io
+
+    from ecoint8 import I8Linear
+
+    lin = I8Linear(8, 4)
+    v0 = lin.sw.version
+    lin.sw[0] = 0.5
+    lin.sw += [0.1]
+    lin.sw.pop()
+    assert lin.sw.version == v0 + 3 and isinstance(lin.sw, list)
+    lin.sw = [1.0, 2.0, 3.0, 4.0]
+    assert lin.sw == [1.0, 2.0, 3.0, 4.0] and hasattr(lin.sw, "version")
+    buf = io.BytesIO()
+    torch.save(lin, buf)
+    buf.seek(0)
+    back = torch.load(buf, weights_only=False)
+    assert back.sw == [1.0, 2.0, 3.0, 4.0] and torch.equal(back.w_i8, lin.w_i8)
+
+
+def test_replay_sites_follow_reference_order_without_gpu():
+    """Replay mode asks the draw function in the reference's order with its shapes/denominators."""
+    from ecoint8 import _sr
+
+    calls = []
+
+    def fn(shape, denom, device):
+        calls.append((tuple(shape), denom))
+        return torch.zeros(tuple(shape), dtype=torch.int32)
+
+    with _sr.replay(fn):
+        s1 = _sr.draw((4, 5), 12, torch.device("cpu"), batch=True)
+        s2 = _sr.draw((4, 5), -3, torch.device("cpu"), batch=True)  # left shift: no draw
+    assert calls == [((4, 5), 4096)] and s1.nudge is not None and s2.nudge is None
