@@ -309,7 +309,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
+    ap.add_argument("--only", choices=["gemm", "eco_step"], help="run one side measurement alone (profiling)")
     args = ap.parse_args()
+    if args.only:
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        res = gemm_measurements(dev)[0] if args.only == "gemm" else eco_step_measurement(dev)
+        print(json.dumps({args.only: res}))
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
