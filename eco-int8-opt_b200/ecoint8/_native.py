@@ -55,6 +55,8 @@ _SIGS = {
     "eco_device_supported": (c_i32, [c_i32]),
     "eco_gemm_s8s32": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_p, c_i64, c_p,
                                c_p]),
+    "eco_gemm_s8s32_noalloc": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_p, c_i64,
+                                       c_p, c_p]),
     "eco_gemm_s8_requant": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_p, c_i32,
                                     c_i32, SRSpec, c_p, c_i64, c_p]),
     "eco_requant_s32_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_p, c_i64, c_i32, c_i32, SRSpec, c_p, c_i64,

@@ -81,6 +81,21 @@ ECO_API int eco_gemm_s8s32(const int8_t* A, int64_t lda, int a_layout, const int
                    int b_layout, int64_t M, int64_t N, int64_t K, const int32_t* bias, int32_t* C,
                    int64_t ldc, int32_t* amax, eco_stream_t stream);
 
+/* eco_gemm_s8s32 for callers that cannot allocate device memory (code running
+ * under stream capture, runtimes that plan every buffer ahead, plain C hosts
+ * without a caching allocator).  A and B need not follow the 16-byte rule: an
+ * operand that breaks it is copied into a 32 MiB buffer the library keeps in
+ * file-scope device memory (held by every GPU that loads it, until exit),
+ * never into memory the call allocates.  A relayout larger than 32 MiB is
+ * rejected with ECO_ERR_ARG.  All calls share that buffer, so calls that
+ * overlap on the GPU race; the first call on a device looks the buffer up and
+ * should come before any stream capture.  No counterpart in the reference
+ * (its torch._int_mm path pads into freshly allocated tensors). */
+ECO_API int eco_gemm_s8s32_noalloc(const int8_t* A, int64_t lda, int a_layout, const int8_t* B,
+                                   int64_t ldb, int b_layout, int64_t M, int64_t N, int64_t K,
+                                   const int32_t* bias, int32_t* C, int64_t ldc, int32_t* amax,
+                                   eco_stream_t stream);
+
 /* Y = sat8(relu?( SR((C + bias[n]) * mult[n], shift) )) fused in the GEMM epilogue.
  * Replaces ilayer.py:135-141 (_int_mm + b_acc + _common_shift_requant :57-70) and,
  * with relu=1, the I8ReLU.apply_forward clamp that follows (:180-182). */
