@@ -1,21 +1,28 @@
 // int8 x int8 -> int32 GEMM on sm_100a tensor cores (tcgen05.mma kind::i8).
 //
-// One CTA computes one 128 x BN output tile.  Warp roles (192 threads):
-//   warp 0     TMA producer: one thread streams 128-deep K slices of A and B
-//              into an S-stage shared-memory ring (128-byte swizzle);
-//   warp 1     owns the TMEM accumulator (alloc / dealloc) and one thread issues
-//              tcgen05.mma (M=128, N=BN, K=32) four times per slice;
-//   warps 2-5  epilogue: tcgen05.ld the int32 accumulator (one row per thread),
-//              then either store int32 + track max|C| (dX, dW, calibration) or
+// Persistent kernel: one CTA per SM walks a grouped order of 128 x BN output
+// tiles.  Warp roles (320 threads):
+//   warp 0     TMA producer: one thread streams 128-deep K slices of A and B into
+//              an S-stage shared-memory ring (128-byte swizzle), across tiles;
+//   warp 1     owns TMEM (2 x BN columns: a double-buffered accumulator) and one
+//              thread issues tcgen05.mma (M=128, N=BN, K=32) four times per slice
+//              into the buffer the epilogue is not draining;
+//   warps 2-9  epilogue: two warps per TMEM lane quarter, each on half of the
+//              columns, tcgen05.ld the int32 accumulator (one row per thread) and
+//              either store int32 + track max|C| (dX, dW, calibration) or
 //              requantize in registers -- bias add, per-column multiplier,
 //              stochastic rounding, ReLU, int8 saturation -- and store int8, so
-//              the forward's int32 accumulator never reaches HBM.
+//              the forward's int32 accumulator never reaches HBM.  Then they
+//              release the buffer, and the epilogue of tile i overlaps the
+//              MMAs of tile i+1.
 // Both operand majors are native: a K-major tile is a [rows][128 B] TMA box,
 // an MN-major tile is one or two [128 K rows][128 B] boxes, described to the
 // MMA by the canonical SWIZZLE_128B K-major / MN-major shared-memory layouts.
+// No TMA multicast (the kernels also run in multi-GPU jobs).
 // Every mbarrier wait is bounded by %globaltimer: on expiry the thread records
-// ECO_FLAG_WAIT_TIMEOUT in a device word, in-flight copies are drained with a
-// bounded wait, TMEM is freed and the CTA returns.
+// ECO_FLAG_WAIT_TIMEOUT in a device word and raises the CTA's abort flag, the
+// roles leave their loops, in-flight copies and MMAs are drained with bounded
+// waits, TMEM is freed and the CTA returns.
 #include <cuda.h>
 
 #include <algorithm>
@@ -29,20 +36,24 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes = int8 elements per K slice (one 128-byte swizzle row)
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s bound on any single wait
+constexpr int kGroupM = 16;                            // M tiles per raster group (L2 reuse)
 
 template <int BN>
 struct Cfg {
   static constexpr int S = BN == 256 ? 4 : 6;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
-  static constexpr int SMEM = S * (A_BYTES + B_BYTES) + 1024 /*barriers etc*/ + 2 * BN * 4 + 1024 /*align*/;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = S * (A_BYTES + B_BYTES) + 1024 /*barriers*/ + 1024 /*align*/;
 };
 
 struct GemmParams {
   int M, N, K;
   int a_mn, b_mn;
+  int tiles_m, tiles_n;
   const int32_t* bias;
   // int32 epilogue
   int32_t* C;
@@ -56,6 +67,16 @@ struct GemmParams {
   i64 ldy;
 };
 
+// Tile t of the grouped raster: kGroupM M-tiles share each N column block in turn.
+ECO_DEV void tile_coords(const GemmParams& p, int t, int& mb, int& nb) {
+  const int per_group = kGroupM * p.tiles_n;
+  const int g = t / per_group, r = t - g * per_group;
+  const int m_first = g * kGroupM;
+  const int gm = min(kGroupM, p.tiles_m - m_first);
+  mb = m_first + r % gm;
+  nb = r / gm;
+}
+
 ECO_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 ECO_DEV unsigned long long globaltimer() {
   unsigned long long t;
@@ -68,6 +89,9 @@ ECO_DEV void mbar_init(uint64_t* bar, uint32_t count) {
 ECO_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                : "memory");
+}
+ECO_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 ECO_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
@@ -138,6 +162,75 @@ ECO_DEV uint32_t idesc_s8(int n, int a_mn, int b_mn) {
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
+// int32 epilogue for one 32-column chunk of one row: bias add, max|C|, store.
+ECO_DEV void epi_store_s32(const GemmParams& p, const uint32_t (&v)[32], int m, int nb, int bias_lane, i64& amax) {
+  int o[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {
+    o[e] = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
+    const int a = (int)(o[e] < 0 ? 0u - (unsigned)o[e] : (unsigned)o[e]);
+    if (nb + e < p.N && m < p.M) amax = max(amax, (i64)a);
+  }
+  if (m >= p.M) return;
+  int32_t* dst = p.C + (i64)m * p.ldc + nb;
+  if (nb + 32 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) *reinterpret_cast<int4*>(dst + e) = make_int4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (nb + e < p.N) dst[e] = o[e];
+  }
+}
+
+// Fused requant epilogue for one 32-column chunk of one row.
+ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int m, int nb, int bias_lane,
+                               int mult_lane) {
+  uint32_t packed[8];
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    i64 nud[2] = {0, 0};
+    if (p.shift >= 0) {
+      if (p.sr.mode == ECO_SR_NEAREST) {
+        nud[0] = nud[1] = half_nudge(p.shift);
+      } else if (p.sr.mode == ECO_SR_PHILOX) {
+        u64 we, wo;
+        sr_pair(p.sr.seed, p.sr.stream, (uint32_t)(p.sr.row_base + m), (uint32_t)((nb + e) >> 1), we, wo);
+        nud[0] = low_bits(we, p.shift);
+        nud[1] = low_bits(wo, p.shift);
+      } else if (m < p.M) {
+#pragma unroll
+        for (int d = 0; d < 2; ++d) {
+          if (nb + e + d < p.N) {
+            const i64 idx = (i64)m * p.sr.nudge_ld + nb + e + d;
+            nud[d] = p.sr.mode == ECO_SR_REPLAY32 ? (i64) static_cast<const int32_t*>(p.sr.nudge)[idx]
+                                                 : static_cast<const i64*>(p.sr.nudge)[idx];
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < 2; ++d) {
+      const int x = add32((int)v[e + d], __shfl_sync(0xffffffffu, bias_lane, e + d));
+      int8_t y = sat8(ams((i64)x, (i64)__shfl_sync(0xffffffffu, mult_lane, e + d), p.shift, nud[d]));
+      if (p.relu && y < 0) y = 0;
+      const int byte = e + d;
+      if (byte % 4 == 0) packed[byte / 4] = 0;
+      packed[byte / 4] |= (uint32_t)(uint8_t)y << (8 * (byte % 4));
+    }
+  }
+  if (m >= p.M) return;
+  int8_t* dst = p.Y + (i64)m * p.ldy + nb;
+  if (nb + 32 <= p.N && (p.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15) == 0) {
+    *reinterpret_cast<int4*>(dst) = make_int4(packed[0], packed[1], packed[2], packed[3]);
+    *reinterpret_cast<int4*>(dst + 16) = make_int4(packed[4], packed[5], packed[6], packed[7]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (nb + e < p.N) dst[e] = (int8_t)(packed[e / 4] >> (8 * (e % 4)));
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -150,15 +243,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + S * C::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * C::B_BYTES);
   uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  volatile uint32_t* abort_flag = tmem_slot + 1;  // set when the producer or MMA thread timed out
-  int32_t* s_mult = reinterpret_cast<int32_t*>(smem + S * (C::A_BYTES + C::B_BYTES) + 1024);
-  int32_t* s_bias = s_mult + BN;
+  uint64_t* tfull = empty + S;   // [2] accumulator buffer ready for the epilogue
+  uint64_t* tempty = tfull + 2;  // [2] accumulator buffer drained by the epilogue
+  uint64_t* drain = tempty + 2;  // every issued MMA retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;  // a role timed out: everyone leaves
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int num_kb = (p.K + BK - 1) / BK;
+  const int num_tiles = p.tiles_m * p.tiles_n;
 
   if (warp == 0 && lane == 0) {
     *abort_flag = 0u;
@@ -166,22 +259,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps);
+    }
+    mbar_init(drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN));
+                 "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  if (warp >= 2) {
-    for (int i = threadIdx.x - 64; i < BN; i += 128) {
-      const int n = n0 + i;
-      s_bias[i] = (p.bias && n < p.N) ? p.bias[n] : 0;
-      s_mult[i] = (EPI == 1 && n < p.N) ? p.mult[n] : 0;
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -190,142 +280,121 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % S;
-        const uint32_t ph = (uint32_t)(kb / S) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u)) {
-          *abort_flag = 1u;
-          break;
-        }
-        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
-        const int k0 = kb * BK;
-        uint8_t* a_dst = sA + s * C::A_BYTES;
-        uint8_t* b_dst = sB + s * C::B_BYTES;
-        if (p.a_mn)
-          tma_load_2d(a_dst, &tmA, &full[s], m0, k0);
-        else
-          tma_load_2d(a_dst, &tmA, &full[s], k0, m0);
-        if (p.b_mn) {
+      int it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(p, t, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&empty[s], ((uint32_t)(it / S) & 1u) ^ 1u)) {
+            *abort_flag = 1u;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+          const int k0 = kb * BK;
+          uint8_t* a_dst = sA + s * C::A_BYTES;
+          uint8_t* b_dst = sB + s * C::B_BYTES;
+          if (p.a_mn)
+            tma_load_2d(a_dst, &tmA, &full[s], m0, k0);
+          else
+            tma_load_2d(a_dst, &tmA, &full[s], k0, m0);
+          if (p.b_mn) {
 #pragma unroll
-          for (int j = 0; j < BN / 128; ++j) tma_load_2d(b_dst + j * (128 * BK), &tmB, &full[s], n0 + 128 * j, k0);
-        } else {
-          tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d(b_dst + j * (128 * BK), &tmB, &full[s], n0 + 128 * j, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+          }
         }
-        ++issued;
       }
       // drain: every issued copy must land before the CTA can exit
-      for (int kb = issued > S ? issued - S : 0; kb < issued; ++kb) mbar_wait(&full[kb % S], (uint32_t)(kb / S) & 1u);
+      for (int k = it > S ? it - S : 0; k < it; ++k) mbar_wait(&full[k % S], (uint32_t)(k / S) & 1u);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_s8(BN, p.a_mn, p.b_mn);
       const uint32_t a_kstep = p.a_mn ? 32 * 128 : 32, b_kstep = p.b_mn ? 32 * 128 : 32;
       const uint32_t a_lbo = p.a_mn ? 128 * BK : 16, b_lbo = p.b_mn ? 128 * BK : 16;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % S;
-        if (!mbar_wait(&full[s], (uint32_t)(kb / S) & 1u)) {
+      int it = 0, j = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&tempty[b], ((uint32_t)(j >> 1) & 1u) ^ 1u)) {
           *abort_flag = 1u;
           break;
         }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(sA + s * C::A_BYTES), b_base = smem_u32(sB + s * C::B_BYTES);
+        const uint32_t d_tmem = tmem + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (uint32_t)(it / S) & 1u)) {
+            *abort_flag = 1u;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * C::A_BYTES), b_base = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 32; ++kk) {
-          umma_s8(tmem, smem_desc(a_base + kk * a_kstep, a_lbo, 1024), smem_desc(b_base + kk * b_kstep, b_lbo, 1024),
-                  idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < BK / 32; ++kk)
+            umma_s8(d_tmem, smem_desc(a_base + kk * a_kstep, a_lbo, 1024),
+                    smem_desc(b_base + kk * b_kstep, b_lbo, 1024), idesc, (kb | kk) != 0);
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (!ok) break;
+        umma_commit(&tfull[b]);
       }
-      umma_commit(accum);  // also on an early exit: marks every issued MMA retired
+      umma_commit(drain);  // arrives once every MMA issued above has retired
+      mbar_wait(drain, 0);
     }
   } else {
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
-    const int m = m0 + row;
-    const bool ok = mbar_wait(accum, 0) && *abort_flag == 0u;
-    tc_fence_after();
-    if (ok && num_kb > 0) {
-      i64 amax = 0;
-      for (int ch = 0; ch < BN / 32; ++ch) {
+    const int e = warp - 2;
+    const int q = warp & 3;           // TMEM lane quarter this warp may access
+    const int half = e >> 2;          // which half of the BN columns
+    constexpr int kChunks = BN / 64;  // 32-column chunks per half
+    i64 amax = 0;
+    int j = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&tfull[b], (uint32_t)(j >> 1) & 1u) || *abort_flag) {
+        *abort_flag = 1u;
+        break;
+      }
+      tc_fence_after();
+      int mb, nb_t;
+      tile_coords(p, t, mb, nb_t);
+      const int m = mb * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        const int col = half * (BN / 2) + c * 32;
+        const int nb = nb_t * BN + col;
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ch * 32), v);
-        const int nb = n0 + ch * 32;
-        if (nb >= p.N) continue;  // warp-uniform: whole chunk beyond N
+        tmem_ld32(tmem + (uint32_t)(b * BN + col) + ((uint32_t)(q * 32) << 16), v);
+        if (nb >= p.N) continue;  // warp-uniform
+        const int n_lane = nb + lane;
+        const int bias_lane = (p.bias && n_lane < p.N) ? __ldg(p.bias + n_lane) : 0;
         if (EPI == 0) {
-          int o[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            o[e] = add32((int)v[e], s_bias[ch * 32 + e]);
-            const int a = (int)(o[e] < 0 ? 0u - (unsigned)o[e] : (unsigned)o[e]);
-            if (nb + e < p.N && m < p.M) amax = max(amax, (i64)a);
-          }
-          if (m < p.M) {
-            int32_t* dst = p.C + (i64)m * p.ldc + nb;
-            if (nb + 32 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
-#pragma unroll
-              for (int e = 0; e < 32; e += 4) *reinterpret_cast<int4*>(dst + e) = make_int4(o[e], o[e + 1], o[e + 2], o[e + 3]);
-            } else {
-              for (int e = 0; e < 32 && nb + e < p.N; ++e) dst[e] = o[e];
-            }
-          }
+          epi_store_s32(p, v, m, nb, bias_lane, amax);
         } else {
-          uint32_t packed[8];
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            i64 nud[2] = {0, 0};
-            if (p.shift >= 0) {
-              if (p.sr.mode == ECO_SR_NEAREST) {
-                nud[0] = nud[1] = half_nudge(p.shift);
-              } else if (p.sr.mode == ECO_SR_PHILOX) {
-                u64 we, wo;
-                sr_pair(p.sr.seed, p.sr.stream, (uint32_t)(p.sr.row_base + m), (uint32_t)((nb + e) >> 1), we, wo);
-                nud[0] = low_bits(we, p.shift);
-                nud[1] = low_bits(wo, p.shift);
-              } else if (m < p.M) {
-#pragma unroll
-                for (int d = 0; d < 2; ++d) {
-                  if (nb + e + d < p.N) {
-                    const i64 idx = (i64)m * p.sr.nudge_ld + nb + e + d;
-                    nud[d] = p.sr.mode == ECO_SR_REPLAY32 ? (i64) static_cast<const int32_t*>(p.sr.nudge)[idx]
-                                                         : static_cast<const i64*>(p.sr.nudge)[idx];
-                  }
-                }
-              }
-            }
-#pragma unroll
-            for (int d = 0; d < 2; ++d) {
-              const int x = add32((int)v[e + d], s_bias[ch * 32 + e + d]);
-              int8_t y = sat8(ams((i64)x, (i64)s_mult[ch * 32 + e + d], p.shift, nud[d]));
-              if (p.relu && y < 0) y = 0;
-              const int byte = e + d;
-              if (byte % 4 == 0) packed[byte / 4] = 0;
-              packed[byte / 4] |= (uint32_t)(uint8_t)y << (8 * (byte % 4));
-            }
-          }
-          if (m < p.M) {
-            int8_t* dst = p.Y + (i64)m * p.ldy + nb;
-            if (nb + 32 <= p.N && (p.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15) == 0) {
-              *reinterpret_cast<int4*>(dst) = make_int4(packed[0], packed[1], packed[2], packed[3]);
-              *reinterpret_cast<int4*>(dst + 16) = make_int4(packed[4], packed[5], packed[6], packed[7]);
-            } else {
-              for (int e = 0; e < 32 && nb + e < p.N; ++e) dst[e] = (int8_t)(packed[e / 4] >> (8 * (e % 4)));
-            }
-          }
+          const int mult_lane = n_lane < p.N ? __ldg(p.mult + n_lane) : 0;
+          epi_store_requant(p, v, m, nb, bias_lane, mult_lane);
         }
       }
-      if (EPI == 0 && p.amax) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+    if (EPI == 0 && p.amax) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = max(amax, (i64)__shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0) atomicMax(p.amax, (int)amax);
-      }
+      for (int o = 16; o > 0; o >>= 1) amax = max(amax, (i64)__shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0 && amax > 0) atomicMax(p.amax, (int)amax);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
   }
 }
 
@@ -370,8 +439,12 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
       return eco_launch_check("gemm: cudaFuncSetAttribute");
     attr_set = true;
   }
-  dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM));
-  kern<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ta, tb, p);
+  GemmParams q = p;
+  q.tiles_m = (p.M + BM - 1) / BM;
+  q.tiles_n = (p.N + BN - 1) / BN;
+  const int tiles = q.tiles_m * q.tiles_n;
+  const int grid = std::min(tiles, eco_num_sms());  // persistent: one CTA per SM
+  kern<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ta, tb, q);
   return eco_launch_check("gemm_s8_kernel");
 }
 
