@@ -310,11 +310,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
     ap.add_argument("--only", choices=["gemm", "eco_step"], help="run one side measurement alone (profiling)")
+    ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
     args = ap.parse_args()
     if args.only:
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
-        res = gemm_measurements(dev)[0] if args.only == "gemm" else eco_step_measurement(dev)
+        res = gemm_measurements(dev)[0] if args.only == "gemm" else eco_step_measurement(dev, layers=args.eco_layers)
         print(json.dumps({args.only: res}))
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -75,6 +75,57 @@ ECO_DEV u64 sr_word(u64 seed, u64 stream, uint32_t row, uint32_t col) {
   return (col & 1) ? o : e;
 }
 
+// The library's 32-bit stochastic-rounding field of element (row, col): word
+// col & 3 of the Philox call with counter (col >> 2, row, stream_lo, stream_hi).
+// One call serves four consecutive columns.
+constexpr u64 kAltStream = 1ull << 63;  // a site's tie-break stream: its id with the top bit set
+ECO_DEV Philox4 sr_quad(u64 seed, u64 stream, uint32_t row, uint32_t quad) {
+  return philox10(quad, row, (uint32_t)stream, (uint32_t)(stream >> 32), (uint32_t)seed, (uint32_t)(seed >> 32));
+}
+ECO_DEV uint32_t quad_word(const Philox4& o, int k) { return k == 0 ? o.x : (k == 1 ? o.y : (k == 2 ? o.z : o.w)); }
+ECO_DEV uint32_t sr_field(u64 seed, u64 stream, uint32_t row, uint32_t col) {
+  return quad_word(sr_quad(seed, stream, row, col >> 2), col & 3);
+}
+
+// floor((p + u) / 2^c), 0 <= c <= 62, for the stream's nudge u of one element,
+// with int64 wrap-around like the reference.  u's top bits are the element's
+// field f; for c > 32 its low c-32 bits are the tie-break stream's field, which
+// only matters when bits [c-32, c) of p + (f << (c-32)) are all ones (adding
+// fewer than 2^(c-32) can only then carry into bit c): probability 2^-32.
+static __device__ __noinline__ i64 sr_round_tie(i64 p2, int c, u64 seed, u64 stream, uint32_t row, uint32_t col) {
+  const int lo = c - 32;
+  const uint32_t t = sr_field(seed, stream | kAltStream, row, col);
+  return sar64(add64(p2, (i64)(t & ((1u << lo) - 1u))), c);
+}
+ECO_DEV i64 sr_round(i64 p, int c, uint32_t f, u64 seed, u64 stream, uint32_t row, uint32_t col) {
+  if (c <= 32) {
+    const u64 u = c == 32 ? (u64)f : (u64)(f & ((1u << c) - 1u));
+    return sar64(add64(p, (i64)u), c);
+  }
+  const int lo = c - 32;
+  const i64 p2 = add64(p, (i64)((u64)f << lo));
+  if ((uint32_t)((u64)p2 >> lo) != 0xFFFFFFFFu) return p2 >> c;
+  return sr_round_tie(p2, c, seed, stream, row, col);
+}
+
+// The I8ECO step's momentum rounding: u's top 20 bits are bits 12..31 of the
+// element's field (bits 0..11 are the weight nudge); for c > 20 the low c-20
+// bits come from the tie-break stream's 64-bit word, needed only when bits
+// [c-20, c) of p + (top << (c-20)) are all ones (probability 2^-20).
+static __device__ __noinline__ i64 step_m_round_tie(i64 p2, int c, u64 seed, u64 stream, uint32_t row, uint32_t col) {
+  const int lo = c - 20;
+  const u64 t = sr_word(seed, stream | kAltStream, row, col);
+  return sar64(add64(p2, (i64)(t & ((1ull << lo) - 1ull))), c);
+}
+ECO_DEV i64 step_m_round(i64 p, int c, uint32_t field, u64 seed, u64 stream, uint32_t row, uint32_t col) {
+  const uint32_t top = field >> 12;
+  if (c <= 20) return sar64(add64(p, (i64)(top & ((1u << c) - 1u))), c);
+  const int lo = c - 20;
+  const i64 p2 = add64(p, (i64)((u64)top << lo));
+  if ((((u64)p2 >> lo) & 0xFFFFFull) != 0xFFFFFull) return sar64(p2, c);
+  return step_m_round_tie(p2, c, seed, stream, row, col);
+}
+
 // Triton's tl.rand(seed, offset) for an int32 offset: Philox counter
 // (offset, 0, 0, 0); first word as int32, folded to non-negative, times fp32
 // 4.6566127342e-10 (triton/language/random.py, triton 3.6.0).

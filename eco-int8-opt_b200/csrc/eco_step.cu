@@ -103,11 +103,31 @@ struct RowCtx {
   int com_m, com_g, com_mm;
   i64 half_m, half_g;
   i64 b_q, nb_q, lr_q, a_q;
+  bool fast;  // every intermediate of this row fits int32 (see row_is_fast)
 };
 
-// One element of iopt.py:154-176.  Returns new w, new m (int8) and updates row stats.
-ECO_DEV void eco_elem(const RowCtx& c, int w, int m, int g, i64 nw, i64 nm, int8_t& w8, int8_t& m8,
-                      i64& rmax, u64& rsum) {
+// Conservative magnitude bounds of the step's intermediates for |w|,|m|,|g| <= 128
+// (double arithmetic, far from its 2^53 limit at the 2^30 threshold).  When they
+// all stay below 2^30 (|eU| below 2^26) the int32 path with 64-bit products is
+// exactly the reference's int64 arithmetic.
+ECO_DEV bool row_is_fast(const RowCtx& c) {
+  if (c.com_m < 0 || c.com_g < 0 || c.com_mm < 0) return false;
+  const double lim = 1073741824.0;  // 2^30
+  if (c.b_q > INT32_MAX || c.b_q < INT32_MIN || c.nb_q > INT32_MAX || c.nb_q < INT32_MIN || c.lr_q > INT32_MAX ||
+      c.lr_q < INT32_MIN || c.a_q > INT32_MAX || c.a_q < INT32_MIN || c.com_mm > 62)
+    return false;
+  const double bm = (128.0 * (double)c.mult_m + (double)c.half_m) * ldexp(1.0, -c.com_m) + 1.0;
+  const double bg = (128.0 * (double)c.mult_g + (double)c.half_g) * ldexp(1.0, -c.com_g) + 1.0;
+  const double bt = (bm * fabs((double)c.b_q) + bg * fabs((double)c.nb_q)) / 65536.0 + 1.0;
+  const double bth = 128.0 * 4096.0 + bt * fabs((double)c.lr_q) / 65536.0 + 1.0;
+  const double be = bth + 128.0 * 4096.0;
+  const double bn = bt + be * fabs((double)c.a_q) / 65536.0 + 1.0;
+  return bm < lim && bg < lim && bt < lim && bth + 4096.0 < lim && bn < lim && be < 67108864.0;
+}
+
+// One element of iopt.py:154-176 in exact int64 (the reference's arithmetic, wrap-around included).
+ECO_DEV void eco_elem(const RowCtx& c, int w, int m, int g, i64 nw, i64& m_new_out, int8_t& w8, i64& rmax,
+                      u64& rsum) {
   const i64 mU = ams(m, c.mult_m, c.com_m, c.half_m);
   const i64 gU = ams(g, c.mult_g, c.com_g, c.half_g);
   const i64 m_t = sar64(add64(mul64(mU, c.b_q), mul64(gU, c.nb_q)), 16);
@@ -119,33 +139,52 @@ ECO_DEV void eco_elem(const RowCtx& c, int w, int m, int g, i64 nw, i64 nm, int8
   rmax = max(rmax, abs64(m_new));
   rsum += (u64)abs64(eU);
   w8 = (int8_t)wn;
-  m8 = sat8(ams(m_new, c.mult_mm, c.com_mm, nm));
+  m_new_out = m_new;
+}
+
+// Row constants of the int32 path (all fit int32 when row_is_fast holds).
+struct FastRow {
+  int mult_m, mult_g, mult_mm, half_m, half_g, b_q, nb_q, lr_q, a_q;
+  int com_m, com_g, com_mm;
+};
+
+// (int)(x >> s) for 0 <= s <= 63 when the result fits int32: one funnel or one shift.
+ECO_DEV int shr_to_int(i64 x, int s) {
+  const int lo = (int)(uint32_t)x, hi = (int)(x >> 32);
+  return s < 32 ? (int)__funnelshift_r((uint32_t)lo, (uint32_t)hi, s) : (hi >> (s - 32));
+}
+
+// The same element in int32 with 32x32->64 products (only when row_is_fast).
+ECO_DEV void eco_elem_fast(const FastRow& c, int w, int m, int g, int nw, int& m_new_out, int8_t& w8, int& rmax,
+                           int& rsum) {
+  const int mU = shr_to_int((i64)m * c.mult_m + c.half_m, c.com_m);
+  const int gU = shr_to_int((i64)g * c.mult_g + c.half_g, c.com_g);
+  const int m_t = shr_to_int((i64)mU * c.b_q + (i64)gU * c.nb_q, 16);
+  const int thU = (w << 12) - shr_to_int((i64)m_t * c.lr_q, 16);
+  int wn = (thU + nw) >> 12;
+  wn = wn < -127 ? -127 : (wn > 127 ? 127 : wn);
+  const int eU = thU - (wn << 12);
+  const int m_new = m_t + shr_to_int((i64)eU * c.a_q, 16);
+  rmax = max(rmax, abs(m_new));
+  rsum += abs(eU);
+  w8 = (int8_t)wn;
+  m_new_out = m_new;
 }
 
 ECO_DEV i64 replay(const void* p, int bits, i64 idx) {
   return bits == 32 ? (i64)static_cast<const int32_t*>(p)[idx] : static_cast<const i64*>(p)[idx];
 }
 
-// Weight and momentum nudges of one element pair (c even), Philox mode.
-ECO_DEV void philox_nudges(u64 seed, u64 stream, uint32_t row, uint32_t c, int com_mm, i64 (&nw)[2],
-                           i64 (&nm)[2]) {
-  u64 w0, w1;
-  sr_pair(seed, stream, row, c >> 1, w0, w1);
-  nw[0] = (i64)(w0 & 0xFFF);
-  nw[1] = (i64)(w1 & 0xFFF);
-  if (com_mm < 0) {
-    nm[0] = nm[1] = 0;
-  } else if (com_mm <= 52) {
-    nm[0] = low_bits(w0 >> 12, com_mm);
-    nm[1] = low_bits(w1 >> 12, com_mm);
-  } else {
-    u64 a0, a1;
-    sr_pair(seed, stream | (1ull << 63), row, c >> 1, a0, a1);
-    nm[0] = low_bits(a0, com_mm);
-    nm[1] = low_bits(a1, com_mm);
-  }
+// Momentum requant of one element: sat8(SR(m_new * mult_mm, com_mm)) with the site's draw.
+ECO_DEV int8_t m_requant(const RowCtx& c, i64 m_new, bool philox, uint32_t field, i64 nm_replay, u64 seed,
+                         u64 stream, uint32_t row, uint32_t col) {
+  const i64 prod = mul64(m_new, c.mult_mm);
+  if (c.com_mm < 0) return sat8(shl64(prod, -c.com_mm));
+  if (philox) return sat8(step_m_round(prod, c.com_mm, field, seed, stream, row, col));
+  return sat8(sar64(add64(prod, nm_replay), c.com_mm));
 }
 
+template <bool PHILOX>
 __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_constant__ StepParams P) {
   __shared__ double s_wmax[kWarps];
   __shared__ int s_last;
@@ -180,13 +219,20 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
       c.mult_m = row_mult(__ddiv_rn(S.sm4096, sw_o), S.com_m, flags);
       c.mult_g = row_mult(__ddiv_rn(S.sg4096, sw_o), S.com_g, flags);
       c.mult_mm = S.s_m > 0.0 ? row_mult(__ddiv_rn(__ddiv_rn(sw_o, 4096.0), S.s_m), S.com_mm, flags) : 0;
+      c.fast = PHILOX && D.vec && row_is_fast(c);
+      const uint32_t row = (uint32_t)r;
       i64 rmax = INT64_MIN;
       u64 rsum = 0;
       int8_t* wr = L.w + r * L.cols;
       int8_t* mr = L.m + r * L.cols;
       const int8_t* gr = L.g + r * L.cols;
-      const bool philox = H.sr_mode == ECO_SR_PHILOX;
-      if (D.vec) {
+      if (c.fast) {
+        FastRow fr;
+        fr.mult_m = (int)c.mult_m; fr.mult_g = (int)c.mult_g; fr.mult_mm = (int)c.mult_mm;
+        fr.half_m = (int)c.half_m; fr.half_g = (int)c.half_g;
+        fr.b_q = (int)c.b_q; fr.nb_q = (int)c.nb_q; fr.lr_q = (int)c.lr_q; fr.a_q = (int)c.a_q;
+        fr.com_m = c.com_m; fr.com_g = c.com_g; fr.com_mm = c.com_mm;
+        int rmax32 = 0;
         for (i64 j = lane; j < L.cols / 16; j += 32) {
           const i64 c0 = j * 16;
           int4 wv = *reinterpret_cast<const int4*>(wr + c0);
@@ -195,43 +241,45 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
           int8_t* wb = reinterpret_cast<int8_t*>(&wv);
           int8_t* mb = reinterpret_cast<int8_t*>(&mv);
           const int8_t* gb = reinterpret_cast<const int8_t*>(&gv);
+          int rsum32 = 0;
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            i64 nw[2], nm[2];
-            if (philox) {
-              philox_nudges(H.seed, L.stream_w, (uint32_t)r, (uint32_t)(c0 + e), S.com_mm, nw, nm);
-            } else {
-              const i64 idx = r * L.cols + c0 + e;
-              nw[0] = replay(L.nudge_w, 32, idx);
-              nw[1] = replay(L.nudge_w, 32, idx + 1);
-              nm[0] = S.com_mm >= 0 ? replay(L.nudge_m, L.nudge_m_bits, idx) : 0;
-              nm[1] = S.com_mm >= 0 ? replay(L.nudge_m, L.nudge_m_bits, idx + 1) : 0;
+          for (int q = 0; q < 4; ++q) {
+            const Philox4 rnd = sr_quad(H.seed, L.stream_w, row, (uint32_t)((c0 >> 2) + q));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int e = 4 * q + k;
+              const uint32_t f = quad_word(rnd, k);
+              int m_new;
+              int8_t w8;
+              eco_elem_fast(fr, wb[e], mb[e], gb[e], (int)(f & 0xFFFu), m_new, w8, rmax32, rsum32);
+              wb[e] = w8;
+              mb[e] = sat8(step_m_round((i64)m_new * fr.mult_mm, fr.com_mm, f, H.seed, L.stream_w, row,
+                                        (uint32_t)(c0 + e)));
             }
-            eco_elem(c, wb[e], mb[e], gb[e], nw[0], nm[0], wb[e], mb[e], rmax, rsum);
-            eco_elem(c, wb[e + 1], mb[e + 1], gb[e + 1], nw[1], nm[1], wb[e + 1], mb[e + 1], rmax, rsum);
           }
+          rsum += (u64)(unsigned)rsum32;
           *reinterpret_cast<int4*>(wr + c0) = wv;
           *reinterpret_cast<int4*>(mr + c0) = mv;
         }
+        rmax = rmax32;
       } else {
-        for (i64 c0 = 2 * lane; c0 < L.cols; c0 += 64) {
-          i64 nw[2], nm[2];
-          if (philox) {
-            philox_nudges(H.seed, L.stream_w, (uint32_t)r, (uint32_t)c0, S.com_mm, nw, nm);
-          }
+        // exact int64 path: any shape, any alignment, replay mode, wide intermediates
+        for (i64 c0 = 4 * lane; c0 < L.cols; c0 += 128) {
+          Philox4 rnd{0u, 0u, 0u, 0u};
+          if (PHILOX) rnd = sr_quad(H.seed, L.stream_w, row, (uint32_t)(c0 >> 2));
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const i64 col = c0 + e;
+          for (int k = 0; k < 4; ++k) {
+            const i64 col = c0 + k;
             if (col >= L.cols) break;
-            if (!philox) {
-              const i64 idx = r * L.cols + col;
-              nw[e] = replay(L.nudge_w, 32, idx);
-              nm[e] = S.com_mm >= 0 ? replay(L.nudge_m, L.nudge_m_bits, idx) : 0;
-            }
-            int8_t w8, m8;
-            eco_elem(c, wr[col], mr[col], gr[col], nw[e], nm[e], w8, m8, rmax, rsum);
+            const i64 idx = r * L.cols + col;
+            const uint32_t f = quad_word(rnd, k);
+            const i64 nw = PHILOX ? (i64)(f & 0xFFFu) : replay(L.nudge_w, 32, idx);
+            const i64 nm = (!PHILOX && S.com_mm >= 0) ? replay(L.nudge_m, L.nudge_m_bits, idx) : 0;
+            i64 m_new;
+            int8_t w8;
+            eco_elem(c, wr[col], mr[col], gr[col], nw, m_new, w8, rmax, rsum);
             wr[col] = w8;
-            mr[col] = m8;
+            mr[col] = m_requant(c, m_new, PHILOX, f, nm, H.seed, L.stream_w, row, (uint32_t)col);
           }
         }
       }
@@ -250,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
           const i64 mb = row_mult(__ddiv_rn(S.lr_sgb, __dmul_rn(L.sx, sw_o)), S.com_b, flags);
           i64 nb = 0;
           if (S.com_b >= 0) {
-            nb = philox ? low_bits(sr_word(H.seed, L.stream_b, (uint32_t)r, 0u), S.com_b)
+            nb = PHILOX ? low_bits(sr_word(H.seed, L.stream_b, row, 0u), S.com_b)
                         : replay(L.nudge_b, L.nudge_b_bits, r);
           }
           const int delta = (int)ams(L.gb_sum[r], mb, S.com_b, nb);
@@ -329,9 +377,15 @@ extern "C" int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, con
     }
     P.total_tiles = tiles;
     int occ = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, i8eco_step_kernel, kThreads, 0);
+    if (replay)
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, i8eco_step_kernel<false>, kThreads, 0);
+    else
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, i8eco_step_kernel<true>, kThreads, 0);
     const i64 grid = std::max<i64>(1, std::min<i64>(tiles, (i64)eco_num_sms() * std::max(occ, 1)));
-    i8eco_step_kernel<<<(unsigned)grid, kThreads, 0, s>>>(P);
+    if (replay)
+      i8eco_step_kernel<false><<<(unsigned)grid, kThreads, 0, s>>>(P);
+    else
+      i8eco_step_kernel<true><<<(unsigned)grid, kThreads, 0, s>>>(P);
     if (int rc = eco_launch_check("eco_i8eco_step")) return rc;
   }
   return ECO_OK;

@@ -183,40 +183,42 @@ ECO_DEV void epi_store_s32(const GemmParams& p, const uint32_t (&v)[32], int m, 
   }
 }
 
-// Fused requant epilogue for one 32-column chunk of one row.
+// Fused requant epilogue for one 32-column chunk of one row: one Philox call per
+// four columns (the element's 32-bit field; exact tie-break draws only when needed).
 ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int m, int nb, int bias_lane,
                                int mult_lane) {
   uint32_t packed[8];
+  const uint32_t row = (uint32_t)(p.sr.row_base + m);
+  const bool philox = p.sr.mode == ECO_SR_PHILOX && p.shift >= 0;
 #pragma unroll
-  for (int e = 0; e < 32; e += 2) {
-    i64 nud[2] = {0, 0};
-    if (p.shift >= 0) {
-      if (p.sr.mode == ECO_SR_NEAREST) {
-        nud[0] = nud[1] = half_nudge(p.shift);
-      } else if (p.sr.mode == ECO_SR_PHILOX) {
-        u64 we, wo;
-        sr_pair(p.sr.seed, p.sr.stream, (uint32_t)(p.sr.row_base + m), (uint32_t)((nb + e) >> 1), we, wo);
-        nud[0] = low_bits(we, p.shift);
-        nud[1] = low_bits(wo, p.shift);
-      } else if (m < p.M) {
+  for (int q = 0; q < 8; ++q) {
+    Philox4 rnd{0u, 0u, 0u, 0u};
+    if (philox) rnd = sr_quad(p.sr.seed, p.sr.stream, row, (uint32_t)((nb >> 2) + q));
+    packed[q] = 0u;
 #pragma unroll
-        for (int d = 0; d < 2; ++d) {
-          if (nb + e + d < p.N) {
-            const i64 idx = (i64)m * p.sr.nudge_ld + nb + e + d;
-            nud[d] = p.sr.mode == ECO_SR_REPLAY32 ? (i64) static_cast<const int32_t*>(p.sr.nudge)[idx]
-                                                 : static_cast<const i64*>(p.sr.nudge)[idx];
-          }
+    for (int k = 0; k < 4; ++k) {
+      const int e = 4 * q + k;
+      const int x = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
+      const i64 prod = (i64)x * (i64)__shfl_sync(0xffffffffu, mult_lane, e);  // 32x32->64, exact
+      i64 yv;
+      if (p.shift < 0) {
+        yv = shl64(prod, -p.shift);
+      } else if (philox) {
+        yv = sr_round(prod, p.shift, quad_word(rnd, k), p.sr.seed, p.sr.stream, row, (uint32_t)(nb + e));
+      } else if (p.sr.mode == ECO_SR_NEAREST) {
+        yv = sar64(add64(prod, half_nudge(p.shift)), p.shift);
+      } else {
+        i64 nud = 0;
+        if (m < p.M && nb + e < p.N) {
+          const i64 idx = (i64)m * p.sr.nudge_ld + nb + e;
+          nud = p.sr.mode == ECO_SR_REPLAY32 ? (i64) static_cast<const int32_t*>(p.sr.nudge)[idx]
+                                            : static_cast<const i64*>(p.sr.nudge)[idx];
         }
+        yv = sar64(add64(prod, nud), p.shift);
       }
-    }
-#pragma unroll
-    for (int d = 0; d < 2; ++d) {
-      const int x = add32((int)v[e + d], __shfl_sync(0xffffffffu, bias_lane, e + d));
-      int8_t y = sat8(ams((i64)x, (i64)__shfl_sync(0xffffffffu, mult_lane, e + d), p.shift, nud[d]));
+      int8_t y = sat8(yv);
       if (p.relu && y < 0) y = 0;
-      const int byte = e + d;
-      if (byte % 4 == 0) packed[byte / 4] = 0;
-      packed[byte / 4] |= (uint32_t)(uint8_t)y << (8 * (byte % 4));
+      packed[q] |= (uint32_t)(uint8_t)y << (8 * k);
     }
   }
   if (m >= p.M) return;

@@ -48,27 +48,14 @@ ECO_DEV i64 replay_nudge(const eco_sr_t& sr, i64 r, i64 c) {
                                     : static_cast<const i64*>(sr.nudge)[idx];
 }
 
-// Nudges for 16 consecutive columns c0..c0+15 (c0 even) of row r.
-ECO_DEV void nudges16(const eco_sr_t& sr, int shift, i64 r, i64 c0, i64 cols, i64 (&n)[16]) {
-  if (shift < 0) {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) n[e] = 0;
-  } else if (sr.mode == ECO_SR_NEAREST) {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) n[e] = half_nudge(shift);
-  } else if (sr.mode == ECO_SR_PHILOX) {
-    const uint32_t row = (uint32_t)(sr.row_base + r);
-#pragma unroll
-    for (int e = 0; e < 16; e += 2) {
-      u64 we, wo;
-      sr_pair(sr.seed, sr.stream, row, (uint32_t)((c0 + e) >> 1), we, wo);
-      n[e] = low_bits(we, shift);
-      n[e + 1] = low_bits(wo, shift);
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) n[e] = (c0 + e < cols) ? replay_nudge(sr, r, c0 + e) : 0;
-  }
+// floor((p + nudge) / 2^shift) (or p << -shift) for element (r, c) under the
+// site's rounding mode; f is the element's Philox field (Philox mode only).
+ECO_DEV i64 round_elem(const eco_sr_t& sr, int shift, i64 p, i64 r, i64 c, uint32_t f) {
+  if (shift < 0) return shl64(p, -shift);
+  if (sr.mode == ECO_SR_NEAREST) return sar64(add64(p, half_nudge(shift)), shift);
+  if (sr.mode == ECO_SR_PHILOX)
+    return sr_round(p, shift, f, sr.seed, sr.stream, (uint32_t)(sr.row_base + r), (uint32_t)c);
+  return sar64(add64(p, replay_nudge(sr, r, c)), shift);
 }
 
 struct RequantArgs {
@@ -84,12 +71,16 @@ struct RequantArgs {
   int8_t* dst;
   i64 ld_dst;
   i64* sumsq;
+  int mult32;  // mult_scalar fits int32: 32x32->64 products
 };
 
-template <bool VEC>
+// MODE: 0 round half up, 1 Philox, 2 replay.  One thread handles 16 consecutive
+// columns of a row per iteration (one 64-byte load of int32, one 16-byte store).
+template <bool VEC, int MODE>
 __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) {
   const i64 cpr = (a.cols + 15) / 16;
   const i64 total = a.rows * cpr;
+  const bool left = a.shift < 0;
   i64 sq = 0;
   for (i64 t = (i64)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (i64)gridDim.x * blockDim.x) {
     const i64 r = t / cpr;
@@ -106,34 +97,46 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
 #pragma unroll
       for (int e = 0; e < 16; ++e) v[e] = (c0 + e < a.cols) ? a.src[r * a.ld_src + c0 + e] : 0;
     }
-    i64 nud[16];
-    nudges16(a.sr, a.shift, r, c0, a.cols, nud);
-    int8_t o[16];
+    uint32_t packed[4];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const i64 c = c0 + e;
-      const bool in = VEC || c < a.cols;
-      int x = v[e];
-      if (a.bias && in) x = add32(x, a.bias[c]);
-      const i64 mult = a.mult_col ? (in ? (i64)a.mult_col[c] : 0) : a.mult_scalar;
-      int8_t y = sat8(ams((i64)x, mult, a.shift, nud[e]));
-      if (a.relu && y < 0) y = 0;
-      if (a.mask && in && a.mask[r * a.ld_mask + c] <= 0) y = 0;
-      o[e] = in ? y : 0;
-      sq += (i64)y * y * (in ? 1 : 0);
+    for (int q = 0; q < 4; ++q) {
+      Philox4 rnd{0u, 0u, 0u, 0u};
+      if (MODE == 1 && !left)
+        rnd = sr_quad(a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)((c0 >> 2) + q));
+      packed[q] = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = 4 * q + k;
+        const i64 c = c0 + e;
+        const bool in = VEC || c < a.cols;
+        int x = v[e];
+        if (a.bias && in) x = add32(x, a.bias[c]);
+        const i64 prod = a.mult_col ? (i64)x * (i64)(in ? a.mult_col[c] : 0)
+                                    : (a.mult32 ? (i64)x * (i64)(int)a.mult_scalar : mul64((i64)x, a.mult_scalar));
+        i64 yv;
+        if (left)
+          yv = shl64(prod, -a.shift);
+        else if (MODE == 0)
+          yv = sar64(add64(prod, half_nudge(a.shift)), a.shift);
+        else if (MODE == 1)
+          yv = sr_round(prod, a.shift, quad_word(rnd, k), a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r),
+                        (uint32_t)c);
+        else
+          yv = in ? sar64(add64(prod, replay_nudge(a.sr, r, c)), a.shift) : 0;
+        int8_t y = sat8(yv);
+        if (a.relu && y < 0) y = 0;
+        if (a.mask && in && a.mask[r * a.ld_mask + c] <= 0) y = 0;
+        if (!in) y = 0;
+        sq += (i64)y * y;
+        packed[q] |= (uint32_t)(uint8_t)y << (8 * k);
+      }
     }
     if (VEC) {
-      int4 pk;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        w[q] = (uint32_t)(uint8_t)o[4 * q] | ((uint32_t)(uint8_t)o[4 * q + 1] << 8) |
-               ((uint32_t)(uint8_t)o[4 * q + 2] << 16) | ((uint32_t)(uint8_t)o[4 * q + 3] << 24);
-      *reinterpret_cast<int4*>(a.dst + r * a.ld_dst + c0) = pk;
+      *reinterpret_cast<int4*>(a.dst + r * a.ld_dst + c0) = make_int4(packed[0], packed[1], packed[2], packed[3]);
     } else {
 #pragma unroll
       for (int e = 0; e < 16; ++e)
-        if (c0 + e < a.cols) a.dst[r * a.ld_dst + c0 + e] = o[e];
+        if (c0 + e < a.cols) a.dst[r * a.ld_dst + c0 + e] = (int8_t)(packed[e / 4] >> (8 * (e % 4)));
     }
   }
   if (a.sumsq) block_reduce_to<false>(sq, a.sumsq);
@@ -159,16 +162,10 @@ __global__ void __launch_bounds__(kThreads) ams_kernel(const AmsArgs a) {
             : a.x_bits == 32 ? (i64)static_cast<const int32_t*>(a.x)[i]
                              : static_cast<const i64*>(a.x)[i];
     const i64 m = a.mult_kind == 0 ? a.mult_scalar : (a.mult_kind == 1 ? a.mult[c] : a.mult[r]);
-    i64 nud = 0;
-    if (a.shift >= 0) {
-      if (a.sr.mode == ECO_SR_NEAREST)
-        nud = half_nudge(a.shift);
-      else if (a.sr.mode == ECO_SR_PHILOX)
-        nud = low_bits(sr_word(a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)c), a.shift);
-      else
-        nud = replay_nudge(a.sr, r, c);
-    }
-    a.out[i] = ams(x, m, a.shift, nud);
+    const uint32_t f = (a.sr.mode == ECO_SR_PHILOX && a.shift >= 0)
+                           ? sr_field(a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)c)
+                           : 0u;
+    a.out[i] = round_elem(a.sr, a.shift, mul64(x, m), r, c, f);
   }
 }
 
@@ -234,17 +231,27 @@ extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols
     return eco_launch_check("eco_requant_s32_s8 memset");
   if (rows == 0 || cols == 0) return ECO_OK;
   RequantArgs a{src, rows, cols, ld_src, bias_col, mult_col, mult_scalar, shift, relu, sr,
-                mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq)};
+                mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq),
+                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX};
   const bool replay = sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64;
   const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
                    ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0)) &&
                    (!bias_col || eco_aligned16(bias_col)) && (!mult_col || eco_aligned16(mult_col));
   (void)replay;
   const i64 work = rows * ((cols + 15) / 16);
-  if (vec)
-    requant_kernel<true><<<grid_for(work), kThreads, 0, s>>>(a);
-  else
-    requant_kernel<false><<<grid_for(work), kThreads, 0, s>>>(a);
+  const int mode = sr.mode == ECO_SR_NEAREST ? 0 : (sr.mode == ECO_SR_PHILOX ? 1 : 2);
+  const int g = grid_for(work);
+#define ECO_REQUANT_LAUNCH(V, M) requant_kernel<V, M><<<g, kThreads, 0, s>>>(a)
+  if (vec) {
+    if (mode == 0) ECO_REQUANT_LAUNCH(true, 0);
+    else if (mode == 1) ECO_REQUANT_LAUNCH(true, 1);
+    else ECO_REQUANT_LAUNCH(true, 2);
+  } else {
+    if (mode == 0) ECO_REQUANT_LAUNCH(false, 0);
+    else if (mode == 1) ECO_REQUANT_LAUNCH(false, 1);
+    else ECO_REQUANT_LAUNCH(false, 2);
+  }
+#undef ECO_REQUANT_LAUNCH
   return eco_launch_check("eco_requant_s32_s8");
 }
 

@@ -45,61 +45,88 @@ def philox4x32(c0, c1, c2, c3, k0: int, k1: int, rounds: int = 10):
     return c0, c1, c2, c3
 
 
-def sr_word(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
-    """64 random bits for element ``(row, col)`` of stochastic-rounding site ``stream``.
-
-    Counter ``(col >> 1, row, stream_lo, stream_hi)``, key ``(seed_lo, seed_hi)``;
-    an even column takes words ``(x1:x0)``, an odd column ``(x3:x2)``.
-    Returns uint64.
-    """
+def _words(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray, per: int):
+    """Philox outputs for (row, col) with ``per`` columns per call (2: 64-bit, 4: 32-bit words)."""
     rows = np.asarray(rows, dtype=np.uint64)
     cols = np.asarray(cols, dtype=np.uint64)
     rows, cols = np.broadcast_arrays(rows, cols)
-    x0, x1, x2, x3 = philox4x32(cols >> np.uint64(1), rows, stream & 0xFFFFFFFF,
-                                (stream >> 32) & 0xFFFFFFFF, seed & 0xFFFFFFFF,
-                                (seed >> 32) & 0xFFFFFFFF)
+    shift = np.uint64(1 if per == 2 else 2)
+    x = philox4x32(cols >> shift, rows, stream & 0xFFFFFFFF, (stream >> 32) & 0xFFFFFFFF, seed & 0xFFFFFFFF,
+                   (seed >> 32) & 0xFFFFFFFF)
+    return cols, x
+
+
+def sr_word(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
+    """64 random bits for element ``(row, col)`` of site ``stream`` (uint64).
+
+    Counter ``(col >> 1, row, stream_lo, stream_hi)``, key ``(seed_lo, seed_hi)``;
+    an even column takes words ``(x1:x0)``, an odd column ``(x3:x2)``.
+    """
+    cols, (x0, x1, x2, x3) = _words(seed, stream, rows, cols, 2)
     lo = np.where((cols & np.uint64(1)) == 0, x0, x2)
     hi = np.where((cols & np.uint64(1)) == 0, x1, x3)
     return (hi << np.uint64(32)) | lo
 
 
+def sr_field(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
+    """32 random bits for element ``(row, col)``: word ``col & 3`` of counter ``(col >> 2, row, stream)``."""
+    cols, (x0, x1, x2, x3) = _words(seed, stream, rows, cols, 4)
+    k = cols & np.uint64(3)
+    return np.select([k == 0, k == 1, k == 2], [x0, x1, x2], x3).astype(np.uint64)
+
+
 def low_bits(word: np.ndarray, nbits: int) -> np.ndarray:
     """``word mod 2**nbits`` as int64 (0 <= nbits <= 63)."""
     if nbits <= 0:
-        return np.zeros(word.shape, dtype=np.int64)
-    return (word & np.uint64((1 << nbits) - 1)).astype(np.int64)
+        return np.zeros(np.shape(word), dtype=np.int64)
+    return (np.asarray(word, dtype=np.uint64) & np.uint64((1 << nbits) - 1)).astype(np.int64)
+
+
+STREAM_ALT = 1 << 63  # the tie-break stream of a site is its stream id with the top bit set
 
 
 def sr_nudge(seed: int, stream: int, shape, shift: int, row_base: int = 0) -> np.ndarray:
-    """``U[0, 2**shift)`` nudges for a ``[rows, cols]`` site (row index offset by ``row_base``)."""
+    """``U[0, 2**shift)`` nudges of a requant site, ``[rows, cols]`` (rows offset by ``row_base``).
+
+    The top bits are the element's 32-bit field; for ``shift > 32`` the low
+    ``shift - 32`` bits come from the field of the tie-break stream.  The CUDA
+    kernels draw the tie-break field only when the rounding depends on it
+    (probability 2**-32), which gives the same result.
+    """
     rows, cols = (shape if len(shape) == 2 else (int(np.prod(shape[:-1])), shape[-1]))
     r = np.arange(rows, dtype=np.uint64)[:, None] + np.uint64(row_base)
     c = np.arange(cols, dtype=np.uint64)[None, :]
-    return low_bits(sr_word(seed, stream, r, c), shift).reshape(shape)
-
-
-STEP_M_SPLIT = 52  # momentum nudges up to 52 bits share the weight nudge's word
-STREAM_ALT = 1 << 63
+    f = sr_field(seed, stream, r, c)
+    if shift <= 32:
+        u = low_bits(f, shift)
+    else:
+        lo = shift - 32
+        t = low_bits(sr_field(seed, stream | STREAM_ALT, r, c), lo)
+        u = ((f.astype(np.int64) << np.int64(lo)) | t)
+    return u.reshape(shape)
 
 
 def step_nudges(seed: int, stream: int, rows: int, cols: int, com_mm: int):
     """Weight (12-bit) and momentum (``com_mm``-bit) nudges of one I8ECO layer step.
 
-    Both come from one 64-bit word per element: the weight nudge is its low 12
-    bits, the momentum nudge the next ``com_mm`` bits when ``com_mm <= 52``;
-    otherwise the momentum nudge is the low ``com_mm`` bits of the word of
-    stream ``stream | 2**63``.
+    One 32-bit field per element: the weight nudge is its low 12 bits and the
+    momentum nudge's top bits are its high 20 bits; for ``com_mm > 20`` the low
+    ``com_mm - 20`` bits come from the 64-bit word of the tie-break stream
+    (drawn by the kernel only when the rounding depends on them).
     """
     r = np.arange(rows, dtype=np.uint64)[:, None]
     c = np.arange(cols, dtype=np.uint64)[None, :]
-    word = sr_word(seed, stream, r, c)
-    nw = low_bits(word, 12)
+    f = sr_field(seed, stream, r, c)
+    nw = low_bits(f, 12)
+    mf = (f >> np.uint64(12)).astype(np.uint64)
     if com_mm < 0:
         nm = None
-    elif com_mm <= STEP_M_SPLIT:
-        nm = low_bits(word >> np.uint64(12), com_mm)
+    elif com_mm <= 20:
+        nm = low_bits(mf, com_mm)
     else:
-        nm = low_bits(sr_word(seed, stream | STREAM_ALT, r, c), com_mm)
+        lo = com_mm - 20
+        t = low_bits(sr_word(seed, stream | STREAM_ALT, r, c), lo)
+        nm = (mf.astype(np.int64) << np.int64(lo)) | t
     return nw, nm
 
 
