@@ -98,6 +98,15 @@ ECO_DEV i64 row_mult(double r, int com, unsigned& flags) {
   return d >= 31 ? 0 : (i64)(m >> d);
 }
 
+// s_m <- max_o(rowmax_o * sw_o / 4096) / 127 (or 1.0), clear the accumulator (iopt.py:178-180).
+ECO_DEV void finalize_state(i64* st) {
+  const i64 acc = atomicExch(reinterpret_cast<unsigned long long*>(&st[1]), 0ull);
+  const u64 fl = atomicAdd(reinterpret_cast<unsigned long long*>(&st[2]), 0ull);
+  if (fl) return;  // flagged layer keeps its scale
+  const double amax_real = __longlong_as_double(acc);
+  st[0] = __double_as_longlong(amax_real > 0.0 ? __ddiv_rn(amax_real, 127.0) : 1.0);
+}
+
 struct RowCtx {
   i64 mult_m, mult_g, mult_mm;
   int com_m, com_g, com_mm;
@@ -220,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
       c.mult_g = row_mult(__ddiv_rn(S.sg4096, sw_o), S.com_g, flags);
       c.mult_mm = S.s_m > 0.0 ? row_mult(__ddiv_rn(__ddiv_rn(sw_o, 4096.0), S.s_m), S.com_mm, flags) : 0;
       c.fast = PHILOX && D.vec && row_is_fast(c);
-      const uint32_t row = (uint32_t)r;
+      const uint32_t row = (uint32_t)(L.row_base + r);  // global row: shards draw what the whole layer would
       i64 rmax = INT64_MIN;
       u64 rsum = 0;
       int8_t* wr = L.w + r * L.cols;
@@ -324,16 +333,16 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int li = threadIdx.x; li < P.n_layers; li += blockDim.x) {
-    i64* st = reinterpret_cast<i64*>(P.layers[li].L.state);
-    const i64 acc = atomicExch(reinterpret_cast<unsigned long long*>(&st[1]), 0ull);
-    const u64 fl = atomicAdd(reinterpret_cast<unsigned long long*>(&st[2]), 0ull);
-    if (fl) continue;  // flagged layer keeps its scale
-    const double amax_real = __longlong_as_double(acc);
-    const double s_m_new = amax_real > 0.0 ? __ddiv_rn(amax_real, 127.0) : 1.0;
-    st[0] = __double_as_longlong(s_m_new);
+  if (H.finalize) {
+    for (int li = threadIdx.x; li < P.n_layers; li += blockDim.x)
+      finalize_state(reinterpret_cast<i64*>(P.layers[li].L.state));
   }
   if (threadIdx.x == 0) *H.done_counter = 0u;
+}
+
+__global__ void i8eco_finalize_kernel(i64* state, int n_layers) {
+  for (int li = blockIdx.x * blockDim.x + threadIdx.x; li < n_layers; li += gridDim.x * blockDim.x)
+    finalize_state(state + 4 * li);
 }
 
 }  // namespace
@@ -389,4 +398,12 @@ extern "C" int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, con
     if (int rc = eco_launch_check("eco_i8eco_step")) return rc;
   }
   return ECO_OK;
+}
+
+extern "C" int eco_i8eco_finalize(int64_t* state, int n_layers, eco_stream_t stream) {
+  ECO_REQUIRE(state && n_layers >= 0, ECO_ERR_ARG, "eco_i8eco_finalize: bad arguments");
+  if (n_layers == 0) return ECO_OK;
+  i8eco_finalize_kernel<<<(n_layers + 127) / 128, 128, 0, eco_stream(stream)>>>(reinterpret_cast<i64*>(state),
+                                                                               n_layers);
+  return eco_launch_check("eco_i8eco_finalize");
 }

@@ -36,7 +36,7 @@ class I8ECOLayer(ctypes.Structure):
 
     _fields_ = [("w", c_p), ("m", c_p), ("g", c_p), ("sw", c_p), ("rowsum", c_p), ("gsq", c_p), ("state", c_p),
                 ("b_acc", c_p), ("gb_sum", c_p), ("nudge_w", c_p), ("nudge_m", c_p), ("nudge_b", c_p),
-                ("rows", c_i64), ("cols", c_i64), ("sw_min", c_d), ("sw_max", c_d), ("s_g", c_d),
+                ("rows", c_i64), ("cols", c_i64), ("row_base", c_i64), ("sw_min", c_d), ("sw_max", c_d), ("s_g", c_d),
                 ("s_gb", c_d), ("sx", c_d), ("stream_w", c_u64), ("stream_b", c_u64),
                 ("nudge_m_bits", c_i32), ("nudge_b_bits", c_i32)]
 
@@ -45,7 +45,7 @@ class I8ECOHyper(ctypes.Structure):
     """``eco_i8eco_hyper_t``."""
 
     _fields_ = [("lr", c_d), ("grad_clip", c_d), ("b_q", c_i64), ("nb_q", c_i64), ("lr_q", c_i64),
-                ("a_q", c_i64), ("sr_mode", c_i32), ("pad_", c_i32), ("seed", c_u64), ("done_counter", c_p)]
+                ("a_q", c_i64), ("sr_mode", c_i32), ("finalize", c_i32), ("seed", c_u64), ("done_counter", c_p)]
 
 
 # name -> (restype, argtypes); one line per entry point of the header
@@ -68,6 +68,7 @@ _SIGS = {
     "eco_read_device_errors": (c_i32, [ctypes.POINTER(c_u32)]),
     "eco_copy2d_s8": (c_i32, [c_p, c_i64, c_p, c_i64, c_i64, c_i64, c_p]),
     "eco_i8eco_step": (c_i32, [ctypes.POINTER(I8ECOLayer), c_i32, ctypes.POINTER(I8ECOHyper), c_p]),
+    "eco_i8eco_finalize": (c_i32, [c_p, c_i32, c_p]),
     "eco_sgdm_step": (c_i32, [c_p, c_p, c_p, c_i64, c_i64, c_p, c_p, c_f, c_f, c_f, c_f, c_u64, c_p, c_p]),
 }
 

@@ -101,6 +101,22 @@ def draw(shape, shift: int, device, batch: bool, kind: str = "requant") -> Site:
     return Site(nat.sr_spec(nat.SR_PHILOX, seed=key, stream_id=0, row_base=rb), None)
 
 
+def reserve_key() -> int | None:
+    """Take a site's Philox key now and build the site later (None in replay mode)."""
+    if _REPLAY is not None:
+        return None
+    return new_key()
+
+
+def site_from_key(key: int, shape, shift: int, row_base: int, kind: str = "requant") -> Site:
+    """The Philox site of a key taken earlier with ``reserve_key``."""
+    if shift < 0:
+        return Site(nat.sr_spec(nat.SR_NEAREST), None)
+    if LOG is not None:
+        LOG.append((kind, key, 0, tuple(shape), shift, row_base))
+    return Site(nat.sr_spec(nat.SR_PHILOX, seed=key, stream_id=0, row_base=row_base), None)
+
+
 def replay_draw(shape, denom, device) -> torch.Tensor:
     """A raw draw from the active replay function (the step assembles its chunks)."""
     return _REPLAY(torch.Size(shape), denom, device).to(device=device)

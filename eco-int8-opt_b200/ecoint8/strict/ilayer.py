@@ -129,9 +129,26 @@ class I8Linear(nn.Module):
         self.sx: float | None = None
         self.sy: float | None = None
         self._cache_x: torch.Tensor | None = None
-        self._gw_i8: torch.Tensor | None = None
+        self._gw_i8 = None
+        self._gw_rows = None  # (lo, hi) when the stashed gradient is this rank's row shard
+        self._dw_pending = None
         self._fwd_cache = None
         self._sw_cache = None
+
+    # Gradient stashes of the reference (ilayer.py:155-156, 168-169).  Under data
+    # parallelism the dW reduction is still in flight when backward_i8 returns;
+    # reading any of them completes every pending layer at once.
+    def _grad_get(self, name):
+        if self.__dict__.get("_dw_pending") is not None:
+            parallel.finalize_pending()
+        return self.__dict__.get(name + "_store")
+
+    _gw_i8 = property(lambda self: self._grad_get("_gw_i8"),
+                      lambda self, v: self.__dict__.__setitem__("_gw_i8_store", v))
+    _gw_s = property(lambda self: self._grad_get("_gw_s"),
+                     lambda self, v: self.__dict__.__setitem__("_gw_s_store", v))
+    _gb_sum = property(lambda self: self._grad_get("_gb_sum"),
+                       lambda self, v: self.__dict__.__setitem__("_gb_sum_store", v))
 
     # ``sw`` is a list of floats like the reference's; edits invalidate the device copies
     @property
@@ -201,6 +218,7 @@ class I8Linear(nn.Module):
         _check_int(x_i8, "layer input")
         _native.require_cuda(x_i8, self.w_i8)
         assert isinstance(self.sx, float) and isinstance(self.sy, float)
+        parallel.wait_gathers(self)
         mults, com = self._fwd_mults(x_i8.device)
         N, K = x_i8.shape
         out = self.out_features
@@ -223,24 +241,29 @@ class I8Linear(nn.Module):
         dev = _native.require_cuda(g_i8, x_i8, self.w_i8)
         N, out = g_i8.shape
         in_f = x_i8.shape[1]
+        if parallel.active():
+            return self._backward_dp(g_i8, float(s_g), x_i8, _mask, dev)
         amax = torch.empty(2, dtype=torch.int32, device=dev)
         # dW = g^T x: A = g stored [K=N, M=out], B = x stored [K=N, N=in]
         dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N, amax=amax[0:1])
         # dX = g w: A = g [M=N, K=out], B = w stored [K=out, N=in]
         dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax[1:2])
         gb_sum = _ops.colsum(g_i8)
-        if parallel.active():
-            a_dw, a_dx, dw_acc, gb_sum = parallel.reduce_backward(dw_acc, gb_sum, amax)
-        else:
-            a_dw, a_dx = amax.tolist()  # the one host synchronisation of this layer
+        key_w = _sr.reserve_key()  # the dW site's key (data-parallel runs take it at this point too)
+        a_dw, a_dx = amax.tolist()  # the one host synchronisation of this layer
         # dW: exact scales (both per-tensor) -> int8 grad for the optimizer
         s_gw = dynamic_scale_from_int(a_dw, s_g * s_x)
         m_gw, sh_gw = quantize_multiplier((s_g * s_x) / s_gw)
-        site = _requant_site((out, in_f), sh_gw, dev, False, "dw")
+        if key_w is not None:
+            _check_shift(sh_gw, True)
+            site = _sr.site_from_key(key_w, (out, in_f), sh_gw, 0, "dw")
+        else:
+            site = _requant_site((out, in_f), sh_gw, dev, False, "dw")
         self._gw_sumsq = torch.empty(1, dtype=torch.int64, device=dev)
         self._gw_i8 = _ops.requant(dw_acc, m_gw, sh_gw, site, sumsq=self._gw_sumsq)
         self._gw_sumsq_of = self._gw_i8
         self._gw_s = s_gw
+        self._gw_rows = None
         # dX: per-channel s_w approximated by its mean
         sw_mean = sum(self.sw) / len(self.sw)
         s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
@@ -251,6 +274,55 @@ class I8Linear(nn.Module):
         self._gb_sum = gb_sum
         self._gb_s = float(s_g)
         return dx_i8, s_dx
+
+
+    def _backward_dp(self, g_i8, s_g, x_i8, mask, dev):
+        """Data-parallel backward: asynchronous row reduce-scatter of dW (finalized when the
+        gradient is read), global dX maximum over ranks, dX requant.  Same draws and
+        results as the single-device backward on the concatenated batch."""
+        N, out = g_i8.shape
+        in_f = x_i8.shape[1]
+        s_x = self.sx
+        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N)
+        gb_sum = _ops.colsum(g_i8)
+        key_w = _sr.reserve_key()  # the dW site's key, in the reference's draw order
+        parallel.start_dw_reduction(self, dw_acc, gb_sum, s_g)
+        self._dw_pending["key"] = key_w
+        self._gb_s = float(s_g)
+        if key_w is None:  # replay mode draws in order: finish this layer's dW now
+            parallel.finalize_pending()
+        amax_dx = torch.empty(1, dtype=torch.int32, device=dev)
+        dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax_dx)
+        a_dx = parallel.global_max_dx(amax_dx)
+        sw_mean = sum(self.sw) / len(self.sw)
+        s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
+        m_dx, sh_dx = quantize_multiplier((s_g * sw_mean) / s_dx)
+        site = _requant_site((N, in_f), sh_dx, dev, True, "dx")
+        dx_i8 = _ops.requant(dx_acc, m_dx, sh_dx, site, mask=mask)
+        return dx_i8, s_dx
+
+    def _finalize_dw(self, a_dw: int, sumsq_out: torch.Tensor) -> None:
+        """Requantize this rank's rows of the summed dW with the global maximum."""
+        p = self.__dict__["_dw_pending"]
+        self._dw_pending = None
+        s_g, s_x = p["s_g"], self.sx
+        out, in_f = p["full"].shape
+        s_gw = dynamic_scale_from_int(a_dw, s_g * s_x)
+        m_gw, sh_gw = quantize_multiplier((s_g * s_x) / s_gw)
+        _check_shift(sh_gw, True)
+        rows = p["rows"]
+        lo = 0 if rows is None else rows[0]
+        if p.get("key") is not None:
+            site = _sr.site_from_key(p["key"], (out, in_f), sh_gw, lo, "dw")
+        else:
+            site = _sr.draw((out, in_f), sh_gw, p["red"].device, batch=False, kind="dw")
+            if site.nudge is not None and rows is not None:
+                site.nudge = site.nudge[rows[0]:rows[1]].contiguous()
+                site.spec.nudge = site.nudge.data_ptr()
+        self._gw_i8 = _ops.requant(p["red"], m_gw, sh_gw, site, sumsq=sumsq_out)
+        self._gw_s = s_gw
+        self._gw_rows = rows
+        self._gb_sum = p["gb"]
 
 
 class I8ReLU(nn.Module):

@@ -35,7 +35,7 @@ import struct
 import torch
 
 from .. import _native as nat
-from .. import _ops, _sr
+from .. import _ops, _sr, parallel
 from ..fixedpoint import _check_int, quantize_multiplier
 
 __all__ = ["I8ECO"]
@@ -120,6 +120,7 @@ class I8ECO:
     @property
     def stats(self) -> dict:
         if self._pending_stats is not None:
+            parallel.synchronize(self.layers)  # row sums of other ranks (data parallel)
             self._raise_pending(block=True)
             tot_e, n_e = 0.0, 0
             for rowsum, sw, rowlen, out in self._pending_stats:
@@ -197,6 +198,8 @@ class I8ECO:
         keep = []  # tensors that must outlive the launch
         descs = []
         pending = []
+        sharded = []  # (layer, rowsum, rows) stepped on this rank's rows only
+        dp = parallel.active()
         for i, layer in active:
             g_i8 = layer._gw_i8
             _check_int(g_i8, "weight grad")
@@ -206,19 +209,23 @@ class I8ECO:
             m = self.m_i8[i]
             nat.require_cuda(g_i8, w, m)
             g = g_i8.contiguous()
-            if g.dtype != torch.int8 or not (w.is_contiguous() and m.is_contiguous()) or g.shape != w.shape:
+            rows = getattr(layer, "_gw_rows", None)  # this rank's row shard under data parallelism
+            lo, hi = (0, w.shape[0]) if rows is None else rows
+            if (g.dtype != torch.int8 or not (w.is_contiguous() and m.is_contiguous())
+                    or tuple(g.shape) != (hi - lo, w.shape[1])):
                 raise RuntimeError("I8ECO: weights, momentum and gradient must be contiguous int8 of one shape")
-            out, rowlen = g.shape
+            out, rowlen = w.shape
             s_g = float(layer._gw_s)
             sw_bits, sw_min, sw_max = layer._sw_device(dev)
             gsq = self._gsq(layer, g) if self.grad_clip is not None else None
             if self._rowsum[i] is None or self._rowsum[i].numel() != out or self._rowsum[i].device != dev:
                 self._rowsum[i] = torch.empty(out, dtype=torch.int64, device=dev)
             d = nat.I8ECOLayer()
-            d.w, d.m, d.g, d.sw = w.data_ptr(), m.data_ptr(), g.data_ptr(), sw_bits.data_ptr()
-            d.rowsum, d.gsq = self._rowsum[i].data_ptr(), nat.ptr(gsq)
+            d.w, d.m, d.g = w.data_ptr() + lo * rowlen, m.data_ptr() + lo * rowlen, g.data_ptr()
+            d.sw = sw_bits.data_ptr() + 8 * lo
+            d.rowsum, d.gsq = self._rowsum[i].data_ptr() + 8 * lo, nat.ptr(gsq)
             d.state = self._state[i].data_ptr()
-            d.rows, d.cols = out, rowlen
+            d.rows, d.cols, d.row_base = hi - lo, rowlen, lo
             d.sw_min, d.sw_max, d.s_g = sw_min, sw_max, s_g
             d.stream_w, d.stream_b = 2 * i, 2 * i + 1
             d.nudge_m_bits = d.nudge_b_bits = 32
@@ -229,24 +236,33 @@ class I8ECO:
                 com_b = _common_shift([self.lr * s_gb / (layer.sx * sw_min)])  # = min over rows
                 if com_b > 62:  # the reference's torch.randint(0, 2**com_b) raises (iopt.py:194)
                     raise ValueError("Overflow when unpacking long long")
-                d.b_acc, d.gb_sum, d.s_gb, d.sx = layer.b_acc.data_ptr(), gb.data_ptr(), s_gb, layer.sx
+                d.b_acc, d.gb_sum = layer.b_acc.data_ptr() + 4 * lo, gb.data_ptr() + 8 * lo
+                d.s_gb, d.sx = s_gb, layer.sx
                 keep.append(gb)
             if replay:
-                keep += self._replay_nudges(d, layer, s_m_now[i], s_g, gsq, g.shape)
+                keep += self._replay_nudges(d, layer, s_m_now[i], s_g, gsq, (out, rowlen), lo)
             keep += [g, gsq, sw_bits]
             descs.append(d)
             pending.append((self._rowsum[i], list(layer.sw), rowlen, out))
+            if rows is not None:
+                sharded.append((layer, self._rowsum[i], rows))
         hyper = nat.I8ECOHyper()
         hyper.lr = self.lr
         hyper.grad_clip = -1.0 if self.grad_clip is None else float(self.grad_clip)
         hyper.b_q, hyper.nb_q, hyper.lr_q, hyper.a_q = b_q, nb_q, lr_q, a_q
         hyper.sr_mode = nat.SR_REPLAY32 if replay else nat.SR_PHILOX
+        hyper.finalize = 0 if dp else 1  # under data parallelism: max over the row shards first
         hyper.seed = 0 if replay else _sr.new_key()
         hyper.done_counter = self._counter.data_ptr()
         if _sr.LOG is not None and not replay:
             _sr.LOG.append(("i8eco_step", hyper.seed, [(i, 2 * i, 2 * i + 1) for i, _ in active]))
         arr = (nat.I8ECOLayer * len(descs))(*descs)
         nat.call("eco_i8eco_step", arr, len(descs), ctypes.byref(hyper), nat.stream())
+        if dp:
+            parallel.combine_step_state(self._state)
+            nat.call("eco_i8eco_finalize", self._state.data_ptr(), self._state.shape[0], nat.stream())
+            for layer, rowsum, rows in sharded:
+                parallel.gather_rows(layer, rowsum, rows)
         self._pending_stats = pending
         flags = torch.empty(len(self.layers), dtype=torch.int64, pin_memory=True)
         flags.copy_(self._state[:, 2], non_blocking=True)
@@ -255,7 +271,7 @@ class I8ECO:
         self._err = (ev, flags)
         self._keep = keep  # released at the next step (stream-ordered reuse is safe)
 
-    def _replay_nudges(self, d, layer, s_m: float, s_g: float, gsq, shape):
+    def _replay_nudges(self, d, layer, s_m: float, s_g: float, gsq, shape, lo: int = 0):
         """Verification mode: draw in the reference's order (iopt.py:152-197), consume whole.
 
         Host scalars follow the reference expressions; the kernel recomputes the
@@ -278,8 +294,9 @@ class I8ECO:
                 ms.append(_sr.replay_draw((rows, rowlen), 1 << com_mm, dev))
         nw = torch.cat(ws).contiguous()
         nm = torch.cat(ms).contiguous() if ms else torch.zeros(1, dtype=torch.int32, device=dev)
-        d.nudge_w, d.nudge_m = nw.data_ptr(), nm.data_ptr()
         d.nudge_m_bits = 64 if nm.dtype == torch.int64 else 32
+        d.nudge_w = nw.data_ptr() + 4 * lo * rowlen  # a row shard consumes its rows of the layer's draws
+        d.nudge_m = nm.data_ptr() + (d.nudge_m_bits // 8) * lo * rowlen if ms else nm.data_ptr()
         kept = [nw, nm]
         if layer.use_bias:
             com_b = _common_shift([self.lr * float(layer._gb_s) / (layer.sx * sw_o) for sw_o in layer.sw])
@@ -287,8 +304,8 @@ class I8ECO:
                 nb = _sr.replay_draw((out, 1), 1 << com_b, dev).reshape(out).contiguous()
             else:
                 nb = torch.zeros(1, dtype=torch.int32, device=dev)
-            d.nudge_b = nb.data_ptr()
             d.nudge_b_bits = 64 if nb.dtype == torch.int64 else 32
+            d.nudge_b = nb.data_ptr() + ((d.nudge_b_bits // 8) * lo if com_b >= 0 else 0)
             kept.append(nb)
         return kept
 

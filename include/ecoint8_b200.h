@@ -166,7 +166,8 @@ typedef struct {
   const void* nudge_m;    /* replay: [rows, cols] int32/int64 momentum nudges */
   const void* nudge_b;    /* replay: [rows] int32/int64 bias nudges */
   int64_t rows, cols;
-  double sw_min, sw_max;  /* min / max of sw */
+  int64_t row_base;       /* global index of row 0 (a data-parallel row shard; else 0) */
+  double sw_min, sw_max;  /* min / max of sw over ALL rows of the layer */
   double s_g;             /* layer._gw_s */
   double s_gb, sx;        /* layer._gb_s, layer.sx (bias step) */
   uint64_t stream_w;      /* Philox site of the weight / momentum nudges */
@@ -180,13 +181,21 @@ typedef struct {
   double grad_clip;     /* < 0: no clipping (grad_clip=None) */
   int64_t b_q, nb_q, lr_q, a_q; /* iopt.py:107-110 */
   int32_t sr_mode;      /* ECO_SR_PHILOX or a replay mode (replay uses the layer nudges) */
-  int32_t pad_;
+  int32_t finalize;     /* 1: update s_m from the row maxima now; 0: leave the accumulator
+                           (state[1]) for eco_i8eco_finalize, e.g. after a cross-rank max */
   uint64_t seed;
   uint32_t* done_counter; /* device word, zero between steps (reset by the kernel) */
 } eco_i8eco_hyper_t;
 
 ECO_API int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, const eco_i8eco_hyper_t* hyper,
                    eco_stream_t stream);
+
+/* Turns each layer's row-max accumulator into its new momentum scale
+ * (s_m = acc / 127, or 1.0 when the maximum is 0; iopt.py:178-180) and clears the
+ * accumulator; layers with error flags keep their scale.  `state` is
+ * [n_layers, 4] int64 as in eco_i8eco_layer_t.  Used after a step launched with
+ * finalize = 0 once the accumulators hold the maximum over all row shards. */
+ECO_API int eco_i8eco_finalize(int64_t* state, int n_layers, eco_stream_t stream);
 
 /* --------------------------------------------------- EcoInt8SGDM step -----
  * The fused fp32-transient ECO step of EcoInt8SGDM (ecoint8/eco.py:330-362),

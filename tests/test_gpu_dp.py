@@ -92,6 +92,9 @@ def _worker(rank, port, q):
         parallel.init()
         net = _net(dev)
         opt = _train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), 2, lo, 123, 4)
+        parallel.synchronize(net.int8_layers())  # the last step's row all-gathers
+        parallel.gather_momentum(opt)  # momentum rows live on their owner rank
+        stats = opt.stats["mean_abs_e"]
         parallel.shutdown()
         if rank == 0:
             single = _net(dev)
@@ -100,6 +103,7 @@ def _worker(rank, port, q):
             ok &= all(torch.equal(a.b_acc, b.b_acc) for a, b in zip(net.int8_layers(), single.int8_layers()))
             ok &= all(torch.equal(a, b) for a, b in zip(opt.m_i8, sopt.m_i8))
             ok &= opt.s_m == sopt.s_m
+            ok &= stats == sopt.stats["mean_abs_e"]
             q.put(bool(ok))
         dist.barrier()
     finally:
