@@ -218,6 +218,21 @@ def gemm_measurements(device):
             "s32_tops": ops / t_s32 / 1e12, "torch_int_mm_cublas_tops": ops / t_cublas / 1e12}, t_fused, ops
 
 
+def requant_measurement(device, rows=16384, cols=8192):
+    """The dX requant of one 8192-wide layer at batch 16384: int32 -> int8, Philox SR,
+    scalar multiplier, ReLU mask and square sum (4 + 1 + 1 B per element)."""
+    from ecoint8 import _native, _ops, _sr
+
+    gen = torch.Generator(device=device).manual_seed(3)
+    src = torch.randint(-(1 << 24), 1 << 24, (rows, cols), dtype=torch.int32, device=device, generator=gen)
+    mask = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, device=device, generator=gen)
+    sq = torch.empty(1, dtype=torch.int64, device=device)
+    site = _sr.Site(_native.sr_spec(_native.SR_PHILOX, seed=11, stream_id=0), None)
+    t = time_kernel(lambda: _ops.requant(src, 1 << 30, 38, site, mask=mask, sumsq=sq))
+    n = rows * cols
+    return {"shape": [rows, cols], "ms": t * 1e3, "gbs": 6.0 * n / t / 1e9, "bytes_per_element": 6}
+
+
 def eco_step_measurement(device, layers=64, dim=4096, steps=5):
     """Config 4: I8ECO.step over 64 x 4096^2 int8 parameters (w, m, g uniform in [-127, 127])."""
     from ecoint8 import I8ECO, _ops
@@ -309,13 +324,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
-    ap.add_argument("--only", choices=["gemm", "eco_step"], help="run one side measurement alone (profiling)")
+    ap.add_argument("--only", choices=["gemm", "eco_step", "requant"],
+                    help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
+    ap.add_argument("--profile", action="store_true",
+                    help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")
     args = ap.parse_args()
     if args.only:
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
-        res = gemm_measurements(dev)[0] if args.only == "gemm" else eco_step_measurement(dev, layers=args.eco_layers)
+        if args.only == "gemm":
+            res = gemm_measurements(dev)[0]
+        elif args.only == "requant":
+            res = requant_measurement(dev)
+        else:
+            res = eco_step_measurement(dev, layers=args.eco_layers)
         print(json.dumps({args.only: res}))
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -414,6 +437,17 @@ def main():
         torch.cuda.synchronize()
         barrier()
         ms_e2e = e0.elapsed_time(e1)
+        if args.profile:
+            from torch.profiler import ProfilerActivity, profile
+
+            with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+                for _ in range(3):
+                    train_step(net, opt, x_i8, y, world)
+                torch.cuda.synchronize()
+            if rank == 0:
+                print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70),
+                      file=sys.stderr)
+                prof.export_chrome_trace(str(REPO / "gpurun_out" / f"trace_n{world}.json"))
     if world > 1:
         import torch.distributed as dist
 
@@ -440,6 +474,7 @@ def main():
             gm, t_fused, ops = gemm_measurements(device)
             out["gemm"] = gm
             out["eco_step"] = eco_step_measurement(device)
+            out["requant"] = requant_measurement(device)
             achieved = ops / t_fused / 1e12
             out["roofline"] = {"bound": "tensor", "kernel": "gemm_s8_kernel<256,1> (fused forward, 16384x8192x8192)",
                                "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",

@@ -432,6 +432,10 @@ int make_tmap(CUtensorMap* map, const int8_t* base, i64 inner, i64 outer, i64 ld
   return ECO_OK;
 }
 
+// Upper bound on the persistent GEMM's CTAs (0 = one per SM).  A data-parallel
+// caller lowers it so that NCCL's kernels find free SMs and overlap the GEMMs.
+int g_gemm_sm_limit = 0;
+
 template <int BN, int EPI>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
   auto kern = gemm_s8_kernel<BN, EPI>;
@@ -445,7 +449,9 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   q.tiles_m = (p.M + BM - 1) / BM;
   q.tiles_n = (p.N + BN - 1) / BN;
   const int tiles = q.tiles_m * q.tiles_n;
-  const int grid = std::min(tiles, eco_num_sms());  // persistent: one CTA per SM
+  int ctas = eco_num_sms();  // persistent: at most one CTA per SM
+  if (g_gemm_sm_limit > 0) ctas = std::min(ctas, g_gemm_sm_limit);
+  const int grid = std::min(tiles, ctas);
   kern<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ta, tb, q);
   return eco_launch_check("gemm_s8_kernel");
 }
@@ -504,6 +510,12 @@ extern "C" int eco_gemm_s8_requant(const int8_t* A, int64_t lda, int a_layout, c
   p.Y = Y;
   p.ldy = ldy;
   return gemm_common(A, lda, a_layout, B, ldb, b_layout, M, N, K, p, 1, eco_stream(stream), "eco_gemm_s8_requant");
+}
+
+extern "C" int eco_set_gemm_sm_limit(int max_ctas) {
+  ECO_REQUIRE(max_ctas >= 0, ECO_ERR_ARG, "eco_set_gemm_sm_limit: negative limit");
+  g_gemm_sm_limit = max_ctas;
+  return ECO_OK;
 }
 
 extern "C" int eco_read_device_errors(uint32_t* flags) {

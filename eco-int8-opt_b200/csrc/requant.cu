@@ -142,6 +142,87 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
   if (a.sumsq) block_reduce_to<false>(sq, a.sumsq);
 }
 
+// Philox requant of a 16-byte aligned, multiple-of-16-wide matrix, specialized at
+// compile time: MASK (zero where mask <= 0), SUMSQ, COLM (per-column multipliers),
+// BIAS, BIG (shift > 32).  A block walks rows (no index division); a thread takes 16
+// columns per iteration: one 64-byte load, one 16-byte mask load, one 16-byte store,
+// four Philox calls.  0 <= shift <= 62, and with |x * mult| < 2^62 every result of
+// a shift > 32 fits int32, so the tail arithmetic is 32-bit.
+template <bool MASK, bool SUMSQ, bool COLM, bool BIAS, bool BIG>
+__global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantArgs a) {
+  const int cpr = (int)(a.cols >> 4);
+  const int sh = a.shift;
+  const int lo = sh - 32;  // BIG: bits of the tie-break draw
+  const int32_t mult_s = (int32_t)a.mult_scalar;
+  long long sq = 0;
+  for (i64 r = blockIdx.x; r < a.rows; r += gridDim.x) {
+    const uint32_t grow = (uint32_t)(a.sr.row_base + r);
+    const int32_t* srow = a.src + r * a.ld_src;
+    int8_t* drow = a.dst + r * a.ld_dst;
+    // software pipeline: the next chunk's loads are in flight while this one computes
+    int4 nx[4], nm = make_int4(0, 0, 0, 0);
+    int j = threadIdx.x;
+    if (j < cpr) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(srow + j * 16)[q];
+      if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + j * 16);
+    }
+    for (; j < cpr; j += blockDim.x) {
+      const int c0 = j * 16;
+      int v[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[4 * q] = nx[q].x; v[4 * q + 1] = nx[q].y; v[4 * q + 2] = nx[q].z; v[4 * q + 3] = nx[q].w;
+      }
+      const int4 mk = nm;
+      const int jn = j + blockDim.x;
+      if (jn < cpr) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(srow + jn * 16)[q];
+        if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + jn * 16);
+      }
+      const int8_t* mb = reinterpret_cast<const int8_t*>(&mk);
+      uint32_t packed[4];
+      int sq32 = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const Philox4 rnd = sr_quad(a.sr.seed, a.sr.stream, grow, (uint32_t)((c0 >> 2) + q));
+        packed[q] = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int e = 4 * q + k;
+          const int c = c0 + e;
+          int x = v[e];
+          if (BIAS) x = add32(x, a.bias[c]);
+          const i64 prod = (i64)x * (i64)(COLM ? a.mult_col[c] : mult_s);
+          const uint32_t f = quad_word(rnd, k);
+          int y;
+          if (BIG) {
+            const i64 p2 = prod + (i64)((u64)f << lo);
+            const int hi = (int)(p2 >> 32);
+            if (__funnelshift_r((uint32_t)p2, (uint32_t)hi, lo) != 0xFFFFFFFFu)
+              y = hi >> lo;  // (p2 >> shift) fits int32
+            else
+              y = (int)sr_round(prod, sh, f, a.sr.seed, a.sr.stream, grow, (uint32_t)c);
+          } else {
+            const u64 u = sh == 32 ? (u64)f : (u64)(f & ((1u << sh) - 1u));
+            const i64 t = sar64(prod + (i64)u, sh);
+            y = t < -127 ? -127 : (t > 127 ? 127 : (int)t);
+          }
+          y = y < -127 ? -127 : (y > 127 ? 127 : y);
+          if (a.relu && y < 0) y = 0;
+          if (MASK && mb[e] <= 0) y = 0;
+          if (SUMSQ) sq32 += y * y;
+          packed[q] |= (uint32_t)(uint8_t)(int8_t)y << (8 * k);
+        }
+      }
+      if (SUMSQ) sq += sq32;
+      *reinterpret_cast<int4*>(drow + c0) = make_int4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  }
+  if (SUMSQ) block_reduce_to<false>(sq, a.sumsq);
+}
+
 struct AmsArgs {
   const void* x;
   int x_bits;
@@ -240,6 +321,35 @@ extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols
   (void)replay;
   const i64 work = rows * ((cols + 15) / 16);
   const int mode = sr.mode == ECO_SR_NEAREST ? 0 : (sr.mode == ECO_SR_PHILOX ? 1 : 2);
+  const bool mult_ok = mult_col || (mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX);
+  if (vec && mode == 1 && shift >= 0 && mult_ok) {
+    const int gp = (int)std::max<i64>(1, std::min<i64>(rows, (i64)eco_num_sms() * 8));
+    const bool big = shift > 32, m = mask != nullptr, q = sumsq != nullptr, cm = mult_col != nullptr,
+               b = bias_col != nullptr;
+#define ECO_RQP(M, Q, CM, B, BG) requant_philox_kernel<M, Q, CM, B, BG><<<gp, kThreads, 0, s>>>(a)
+#define ECO_RQP_BIG(M, Q, CM, B) \
+  do {                           \
+    if (big) ECO_RQP(M, Q, CM, B, true); else ECO_RQP(M, Q, CM, B, false); \
+  } while (0)
+#define ECO_RQP_B(M, Q, CM) \
+  do {                      \
+    if (b) ECO_RQP_BIG(M, Q, CM, true); else ECO_RQP_BIG(M, Q, CM, false); \
+  } while (0)
+#define ECO_RQP_CM(M, Q) \
+  do {                   \
+    if (cm) ECO_RQP_B(M, Q, true); else ECO_RQP_B(M, Q, false); \
+  } while (0)
+    if (m) {
+      if (q) ECO_RQP_CM(true, true); else ECO_RQP_CM(true, false);
+    } else {
+      if (q) ECO_RQP_CM(false, true); else ECO_RQP_CM(false, false);
+    }
+#undef ECO_RQP_CM
+#undef ECO_RQP_B
+#undef ECO_RQP_BIG
+#undef ECO_RQP
+    return eco_launch_check("eco_requant_s32_s8");
+  }
   const int g = grid_for(work);
 #define ECO_REQUANT_LAUNCH(V, M) requant_kernel<V, M><<<g, kThreads, 0, s>>>(a)
   if (vec) {

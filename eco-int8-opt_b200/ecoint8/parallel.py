@@ -38,10 +38,16 @@ _ACTIVE = False
 _GROUP = None  # large transfers (dW, weights)
 _SMALL = None  # scalar / small-vector collectives
 _PENDING: list = []  # layers whose dW reduction is in flight
+COMM_SMS = 16  # SMs the GEMMs leave free for NCCL while data parallelism is active
 
 
-def init(group=None) -> None:
-    """Enable the exchanges on ``group`` (default: the world).  Collective: call on every rank."""
+def init(group=None, comm_sms: int = COMM_SMS) -> None:
+    """Enable the exchanges on ``group`` (default: the world).  Collective: call on every rank.
+
+    ``comm_sms``: SMs the persistent GEMMs leave to NCCL, so the dW
+    reduce-scatter and the weight all-gather overlap the GEMMs instead of
+    waiting for them to finish.
+    """
     global _ACTIVE, _GROUP, _SMALL
     if not dist.is_initialized():
         raise RuntimeError("ecoint8.parallel.init needs torch.distributed to be initialized")
@@ -49,12 +55,24 @@ def init(group=None) -> None:
     ranks = list(range(dist.get_world_size())) if group is None else dist.get_process_group_ranks(group)
     _SMALL = dist.new_group(ranks=ranks)
     _ACTIVE = True
+    if torch.cuda.is_available() and comm_sms > 0 and len(ranks) > 1:
+        from . import _native
+
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        _native.call("eco_set_gemm_sm_limit", max(1, sms - comm_sms))
 
 
 def shutdown() -> None:
     global _ACTIVE, _GROUP, _SMALL
     finalize_pending()
     _ACTIVE, _GROUP, _SMALL = False, None, None
+    if torch.cuda.is_available():
+        from . import _native
+
+        try:
+            _native.call("eco_set_gemm_sm_limit", 0)
+        except RuntimeError:
+            pass
 
 
 def active() -> bool:
@@ -112,9 +130,7 @@ def start_dw_reduction(layer, dw_acc: torch.Tensor, gb_sum: torch.Tensor, s_g: f
         lo, hi = rows
         red = torch.empty((hi - lo, dw_acc.shape[1]), dtype=dw_acc.dtype, device=dw_acc.device)
         work = dist.reduce_scatter_tensor(red, dw_acc, op=dist.ReduceOp.SUM, group=_GROUP, async_op=True)
-    work_gb = dist.all_reduce(gb_sum, op=dist.ReduceOp.SUM, group=_GROUP, async_op=True)
-    layer._dw_pending = {"red": red, "full": dw_acc, "work": work, "work_gb": work_gb, "gb": gb_sum,
-                         "rows": rows, "s_g": float(s_g)}
+    layer._dw_pending = {"red": red, "full": dw_acc, "work": work, "gb": gb_sum, "rows": rows, "s_g": float(s_g)}
     _PENDING.append(layer)
 
 
@@ -130,10 +146,16 @@ def finalize_pending() -> None:
         return
     layers = list(_PENDING)
     _PENDING.clear()
+    # the bias column sums of every pending layer in one all-reduce
+    gbs = [l._dw_pending["gb"] for l in layers]
+    flat = torch.cat(gbs)
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=_SMALL)
+    off = 0
+    for l, g in zip(layers, gbs):
+        l._dw_pending["gb"] = flat[off:off + g.numel()]
+        off += g.numel()
     for layer in layers:
-        p = layer._dw_pending
-        p["work"].wait()
-        p["work_gb"].wait()
+        layer._dw_pending["work"].wait()
     dev = layers[0].w_i8.device
     maxima = torch.cat([_ops.amax(l._dw_pending["red"]).reshape(1) for l in layers])
     dist.all_reduce(maxima, op=dist.ReduceOp.MAX, group=_SMALL)

@@ -177,6 +177,15 @@ class I8Linear(nn.Module):
             self._fwd_cache = (key, mults, com)
         return self._fwd_cache[1], self._fwd_cache[2]
 
+    def _sw_mean(self) -> float:
+        """``sum(self.sw) / len(self.sw)`` (ilayer.py:160), cached until ``sw`` is edited."""
+        key = self._sw_key()
+        cached = self.__dict__.get("_sw_mean_cache")
+        if cached is None or cached[0] != key:
+            cached = (key, sum(self.sw) / len(self.sw))
+            self.__dict__["_sw_mean_cache"] = cached
+        return cached[1]
+
     def _sw_device(self, device):
         """``sw`` on the device as int64 bit patterns of the doubles, plus its min and max."""
         key = (self._sw_key(), device)
@@ -265,7 +274,7 @@ class I8Linear(nn.Module):
         self._gw_s = s_gw
         self._gw_rows = None
         # dX: per-channel s_w approximated by its mean
-        sw_mean = sum(self.sw) / len(self.sw)
+        sw_mean = self._sw_mean()
         s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
         m_dx, sh_dx = quantize_multiplier((s_g * sw_mean) / s_dx)
         site = _requant_site((N, in_f), sh_dx, dev, True, "dx")
@@ -294,7 +303,7 @@ class I8Linear(nn.Module):
         amax_dx = torch.empty(1, dtype=torch.int32, device=dev)
         dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax_dx)
         a_dx = parallel.global_max_dx(amax_dx)
-        sw_mean = sum(self.sw) / len(self.sw)
+        sw_mean = self._sw_mean()
         s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
         m_dx, sh_dx = quantize_multiplier((s_g * sw_mean) / s_dx)
         site = _requant_site((N, in_f), sh_dx, dev, True, "dx")

@@ -178,7 +178,7 @@ class I8ECO:
     # -- step ------------------------------------------------------------
     @torch.no_grad()
     def step(self):
-        self._raise_pending(block=False)
+        self._raise_pending(block=True)  # the previous step's flags (long since copied back)
         b = self.beta
         alpha = (1.0 / self.lr) * (1.0 - 1.0 / b)
         b_q = round(b * BETA_Q)
@@ -264,9 +264,16 @@ class I8ECO:
             for layer, rowsum, rows in sharded:
                 parallel.gather_rows(layer, rowsum, rows)
         self._pending_stats = pending
-        flags = torch.empty(len(self.layers), dtype=torch.int64, pin_memory=True)
+        # error flags come back asynchronously into one of two persistent pinned buffers
+        # (allocating pinned memory every step can stall the host)
+        if getattr(self, "_flag_bufs", None) is None or self._flag_bufs[0][0].numel() != len(self.layers):
+            self._flag_bufs = [(torch.empty(len(self.layers), dtype=torch.int64, pin_memory=True),
+                                torch.cuda.Event()) for _ in range(2)]
+            self._flag_turn = 0
+        flags, ev = self._flag_bufs[self._flag_turn]
+        self._flag_turn ^= 1
+        ev.synchronize()  # its previous copy finished a step ago
         flags.copy_(self._state[:, 2], non_blocking=True)
-        ev = torch.cuda.Event()
         ev.record()
         self._err = (ev, flags)
         self._keep = keep  # released at the next step (stream-ordered reuse is safe)

@@ -96,6 +96,12 @@ ECO_API int eco_gemm_s8s32_noalloc(const int8_t* A, int64_t lda, int a_layout, c
                                    const int32_t* bias, int32_t* C, int64_t ldc, int32_t* amax,
                                    eco_stream_t stream);
 
+/* Process-wide cap on the CTAs of the persistent GEMM kernels (0, the default: one
+ * per SM).  A data-parallel caller sets it a little below the SM count so that the
+ * collective kernels of NCCL, launched on other streams, find free SMs and overlap
+ * the GEMMs.  No reference counterpart (the reference runs on one device). */
+ECO_API int eco_set_gemm_sm_limit(int max_ctas);
+
 /* Y = sat8(relu?( SR((C + bias[n]) * mult[n], shift) )) fused in the GEMM epilogue.
  * Replaces ilayer.py:135-141 (_int_mm + b_acc + _common_shift_requant :57-70) and,
  * with relu=1, the I8ReLU.apply_forward clamp that follows (:180-182). */
