@@ -327,6 +327,9 @@ def main():
     ap.add_argument("--only", choices=["gemm", "eco_step", "requant"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
+    ap.add_argument("--dw-exchange", default="gather", choices=["gather", "reduce"],
+                    help="how ranks form the summed dW rows (ecoint8.parallel.init)")
+    ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to NCCL under data parallelism")
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")
     args = ap.parse_args()
@@ -382,7 +385,7 @@ def main():
     from ecoint8._sr import batch_rows, set_generator
 
     if world > 1:
-        parallel.init()
+        parallel.init(dw_exchange=args.dw_exchange, comm_sms=args.comm_sms)
     set_generator(torch.Generator().manual_seed(1234))  # identical Philox keys on every rank
     local_b = GLOBAL_BATCH // world
     torch.manual_seed(0)
@@ -466,6 +469,8 @@ def main():
                "config": {"workload": "config 5: deep strict-int8 MLP 8x I8Linear(8192,8192)+I8ReLU, "
                                       "I8Linear(8192,1000); Gaussian inputs, random labels; I8ECO momentum 0.9",
                           "global_batch": GLOBAL_BATCH, "per_gpu_batch": local_b, "parallelism": f"dp{world}",
+                          "dw_exchange": args.dw_exchange if world > 1 else None,
+                          "comm_sms": args.comm_sms if world > 1 else None,
                           "l2": "inputs larger than L2 (1.2 GB activations + 0.55 GB weights); no flush"},
                "e2e": {"value": e2e, "unit": "steps/s", "h2d_bytes_per_step": int(x_i8.numel() + y.numel() * 8),
                        "d2h_bytes_per_step": 4},

@@ -60,3 +60,42 @@ extern "C" int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int
   if (e != cudaSuccess) return eco_fail(ECO_ERR_LAUNCH, "eco_copy2d_s8: %s", cudaGetErrorString(e));
   return ECO_OK;
 }
+
+namespace {
+// dst[p][r][j] = src[r][p * c + j]: 16 bytes per thread when every row and block
+// start is 16-byte aligned, else one byte per thread.
+template <bool VEC>
+__global__ void split_cols_kernel(const int8_t* __restrict__ src, int64_t ld, int64_t rows, int64_t c,
+                                  int64_t parts, int8_t* __restrict__ dst) {
+  const int64_t unit = VEC ? 16 : 1;
+  const int64_t per_row = c / unit;
+  const int64_t total = parts * rows * per_row;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = q / (rows * per_row);
+    const int64_t rem = q - p * rows * per_row;
+    const int64_t r = rem / per_row;
+    const int64_t j = rem - r * per_row;
+    const int8_t* s = src + r * ld + p * c + j * unit;
+    if (VEC)
+      reinterpret_cast<int4*>(dst)[q] = *reinterpret_cast<const int4*>(s);
+    else
+      dst[q] = *s;
+  }
+}
+}  // namespace
+
+extern "C" int eco_split_cols_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int64_t parts,
+                                 int8_t* dst, eco_stream_t stream) {
+  ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && parts > 0 && cols % parts == 0 && ld_src >= cols,
+              ECO_ERR_ARG, "eco_split_cols_s8: bad arguments (cols must divide into parts)");
+  if (rows == 0 || cols == 0) return ECO_OK;
+  const int64_t c = cols / parts;
+  const bool vec = c % 16 == 0 && ld_src % 16 == 0 && eco_aligned16(src) && eco_aligned16(dst);
+  const int64_t units = parts * rows * (vec ? c / 16 : c);
+  const int64_t grid = std::min<int64_t>((units + 255) / 256, (int64_t)eco_num_sms() * 8);
+  if (vec)
+    split_cols_kernel<true><<<(unsigned)grid, 256, 0, eco_stream(stream)>>>(src, ld_src, rows, c, parts, dst);
+  else
+    split_cols_kernel<false><<<(unsigned)grid, 256, 0, eco_stream(stream)>>>(src, ld_src, rows, c, parts, dst);
+  return eco_launch_check("eco_split_cols_s8");
+}

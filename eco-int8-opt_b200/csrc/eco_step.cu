@@ -193,6 +193,38 @@ ECO_DEV int8_t m_requant(const RowCtx& c, i64 m_new, bool philox, uint32_t field
   return sat8(sar64(add64(prod, nm_replay), c.com_mm));
 }
 
+// Bias integer SGD of one row (iopt.py:187-197); r indexes the layer's arrays
+// (global row r + row_base).
+template <bool PHILOX>
+ECO_DEV void bias_update(const eco_i8eco_layer_t& L, const eco_i8eco_hyper_t& H, const LayerScalars& S, i64 r,
+                         double sw_o, unsigned& flags) {
+  const i64 mb = row_mult(__ddiv_rn(S.lr_sgb, __dmul_rn(L.sx, sw_o)), S.com_b, flags);
+  i64 nb = 0;
+  if (S.com_b >= 0) {
+    nb = PHILOX ? low_bits(sr_word(H.seed, L.stream_b, (uint32_t)(L.row_base + r), 0u), S.com_b)
+                : replay(L.nudge_b, L.nudge_b_bits, r);
+  }
+  const int delta = (int)ams(L.gb_sum[r], mb, S.com_b, nb);
+  L.b_acc[r] = (int)((unsigned)L.b_acc[r] - (unsigned)delta);
+}
+
+// The bias step of every global row [0, bias_rows) of the layers that ask for it
+// (a data-parallel row shard), one thread per row; runs before the step kernel,
+// which skips their biases.  A layer whose scalars are flagged is left alone
+// (the step kernel records the flags).
+template <bool PHILOX>
+__global__ void i8eco_bias_kernel(const __grid_constant__ StepParams P) {
+  const eco_i8eco_layer_t& L = P.layers[blockIdx.y].L;
+  const i64 R = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (!L.b_acc || R >= L.bias_rows) return;
+  const LayerScalars S = layer_scalars(L, P.H);
+  if (S.flags) return;
+  const i64 r = R - L.row_base;
+  unsigned flags = 0;
+  bias_update<PHILOX>(L, P.H, S, r, L.sw[r], flags);
+  if (flags) atomicOr(reinterpret_cast<unsigned long long*>(&L.state[2]), (u64)flags);
+}
+
 template <bool PHILOX>
 __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_constant__ StepParams P) {
   __shared__ double s_wmax[kWarps];
@@ -303,16 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
         // r * sw_o / 4096 (iopt.py:178); a negative row max can only come from INT64_MIN
         const double v = __ddiv_rn(__dmul_rn(__ll2double_rn(rmax), sw_o), 4096.0);
         wmax = fmax(wmax, v);
-        if (L.b_acc) {  // bias integer SGD (iopt.py:187-197)
-          const i64 mb = row_mult(__ddiv_rn(S.lr_sgb, __dmul_rn(L.sx, sw_o)), S.com_b, flags);
-          i64 nb = 0;
-          if (S.com_b >= 0) {
-            nb = PHILOX ? low_bits(sr_word(H.seed, L.stream_b, row, 0u), S.com_b)
-                        : replay(L.nudge_b, L.nudge_b_bits, r);
-          }
-          const int delta = (int)ams(L.gb_sum[r], mb, S.com_b, nb);
-          L.b_acc[r] = (int)((unsigned)L.b_acc[r] - (unsigned)delta);
-        }
+        if (L.b_acc && L.bias_rows == 0) bias_update<PHILOX>(L, H, S, r, sw_o, flags);
       }
     }
     if (flags && lane == 0) atomicOr(reinterpret_cast<unsigned long long*>(&L.state[2]), (u64)flags);
@@ -364,6 +387,9 @@ extern "C" int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, con
     ECO_REQUIRE(!L.b_acc || L.gb_sum, ECO_ERR_ARG, "eco_i8eco_step: layer %d: bias needs gb_sum", i);
     ECO_REQUIRE(!replay || (L.nudge_w && L.nudge_m && (!L.b_acc || L.nudge_b)), ECO_ERR_ARG,
                 "eco_i8eco_step: layer %d: replay mode needs nudge tensors", i);
+    ECO_REQUIRE(L.bias_rows == 0 || (L.bias_rows > 0 && L.bias_rows < (1ll << 31) && L.row_base >= 0 &&
+                                      L.row_base + L.rows <= L.bias_rows),
+                ECO_ERR_ARG, "eco_i8eco_step: layer %d: bias_rows must cover the stepped rows", i);
     ECO_REQUIRE(!replay || ((L.nudge_m_bits == 32 || L.nudge_m_bits == 64) &&
                             (!L.b_acc || L.nudge_b_bits == 32 || L.nudge_b_bits == 64)),
                 ECO_ERR_ARG, "eco_i8eco_step: layer %d: nudge widths", i);
@@ -385,6 +411,17 @@ extern "C" int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, con
       tiles += (D.L.rows + D.rows_per_tile - 1) / D.rows_per_tile;
     }
     P.total_tiles = tiles;
+    i64 bias_rows = 0;
+    for (int i = 0; i < P.n_layers; ++i)
+      if (P.layers[i].L.b_acc) bias_rows = std::max<i64>(bias_rows, P.layers[i].L.bias_rows);
+    if (bias_rows > 0) {  // every bias of the data-parallel shards, before their weights
+      const dim3 bgrid((unsigned)((bias_rows + 255) / 256), (unsigned)P.n_layers);
+      if (replay)
+        i8eco_bias_kernel<false><<<bgrid, 256, 0, s>>>(P);
+      else
+        i8eco_bias_kernel<true><<<bgrid, 256, 0, s>>>(P);
+      if (int rc = eco_launch_check("eco_i8eco_step (bias)")) return rc;
+    }
     int occ = 0;
     if (replay)
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, i8eco_step_kernel<false>, kThreads, 0);

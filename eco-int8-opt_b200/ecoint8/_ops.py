@@ -122,3 +122,47 @@ def sumsq(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     out = out if out is not None else torch.empty(1, dtype=_I64, device=x.device)
     nat.call("eco_sumsq_s8", x.data_ptr(), x.numel(), out.data_ptr(), nat.stream())
     return out
+
+
+# -- host reads that do not drain the stream ------------------------------------------
+class PendingRead:
+    """A small device tensor on its way to the host (``read_later``)."""
+
+    __slots__ = ("host", "event")
+
+    def __init__(self, host: torch.Tensor, event):
+        self.host, self.event = host, event
+
+    def value(self) -> list[int]:
+        self.event.synchronize()
+        return self.host.tolist()
+
+
+_SIDE: dict = {}  # device -> (side stream, ring of pinned slots, ring position)
+
+
+def read_later(t: torch.Tensor, work=None) -> PendingRead:
+    """Start copying a small device tensor to the host on a side stream that waits only
+    for the work queued so far on the current stream (and for ``work``, a collective's
+    handle): kernels queued after this call keep the device busy while the host waits
+    in ``PendingRead.value()``."""
+    if t.numel() * t.element_size() > 64:
+        raise ValueError("read_later: at most 64 bytes")
+    dev = t.device
+    ent = _SIDE.get(dev)
+    if ent is None:
+        ent = _SIDE[dev] = [torch.cuda.Stream(device=dev),
+                            [(torch.empty(8, dtype=_I64, pin_memory=True), torch.cuda.Event()) for _ in range(16)], 0]
+    side, ring, pos = ent
+    ent[2] = (pos + 1) % len(ring)
+    buf, ev = ring[pos]
+    ev.synchronize()  # the slot's previous read (long finished)
+    host = buf.view(torch.uint8)[:t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        if work is not None:
+            work.wait()
+        host.copy_(t, non_blocking=True)
+        ev.record(side)
+    t.record_stream(side)
+    return PendingRead(host, ev)

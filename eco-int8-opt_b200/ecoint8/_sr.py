@@ -101,19 +101,33 @@ def draw(shape, shift: int, device, batch: bool, kind: str = "requant") -> Site:
     return Site(nat.sr_spec(nat.SR_PHILOX, seed=key, stream_id=0, row_base=rb), None)
 
 
+_RESERVED: dict = {}  # key -> its place in LOG, filled in by site_from_key
+
+
 def reserve_key() -> int | None:
-    """Take a site's Philox key now and build the site later (None in replay mode)."""
+    """Take a site's Philox key now and build the site later (None in replay mode).
+    ``LOG`` keeps the site at the position of the reservation."""
     if _REPLAY is not None:
         return None
-    return new_key()
+    key = new_key()
+    if LOG is not None:
+        _RESERVED[key] = (LOG, len(LOG))
+        LOG.append(None)
+    return key
 
 
 def site_from_key(key: int, shape, shift: int, row_base: int, kind: str = "requant") -> Site:
     """The Philox site of a key taken earlier with ``reserve_key``."""
+    log, pos = _RESERVED.pop(key, (None, None))
     if shift < 0:
+        if log is not None:  # no draw: the site leaves the log
+            log[pos] = ("none", key, 0, tuple(shape), shift, row_base)
         return Site(nat.sr_spec(nat.SR_NEAREST), None)
-    if LOG is not None:
-        LOG.append((kind, key, 0, tuple(shape), shift, row_base))
+    entry = (kind, key, 0, tuple(shape), shift, row_base)
+    if log is not None:
+        log[pos] = entry
+    elif LOG is not None:
+        LOG.append(entry)
     return Site(nat.sr_spec(nat.SR_PHILOX, seed=key, stream_id=0, row_base=row_base), None)
 
 

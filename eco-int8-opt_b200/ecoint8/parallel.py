@@ -13,11 +13,24 @@ maxima), so ``n`` ranks reproduce the single-device run bit for bit:
   all layers at once, one host read for every dW maximum (MAX over the row
   shards), then each rank requantizes only its rows, and the square sums for
   the gradient clip are summed on the device;
-* optimizer (ZeRO-1 style): each rank steps only its rows; the row-max
-  accumulators of the new momentum scale are combined with a MAX and finalized
-  on the device; the updated int8 weights, int32 biases and row sums are
-  all-gathered asynchronously, and a layer's next forward waits for its own.
+* optimizer (ZeRO-1 style): each rank steps only its weight rows (every rank
+  steps every bias, which needs no weights); the row-max accumulators of the
+  new momentum scale are combined with a MAX and finalized on the device; the
+  updated int8 weights are all-gathered asynchronously, one collective per
+  layer, and a layer's next forward waits for its own; the per-row |e| sums of
+  all layers travel in one more all-gather.
 * calibration: the forward max|acc| is a MAX across ranks.
+
+Two ways of forming the summed dW rows (``init(dw_exchange=...)``):
+
+* ``"reduce"``: every rank computes dW over its own batch rows and the int32
+  accumulators are reduce-scattered by rows (4 bytes per dW element cross
+  NVLink);
+* ``"gather"``: the int8 layer inputs are all-gathered during the forward and the
+  int8 dY column blocks are exchanged all-to-all in the backward, so each rank
+  computes its own dW rows over the whole global batch in one GEMM (the same
+  exact int32 sums; about half the bytes of the reduce-scatter, and no full-size
+  int32 dW in HBM).  Needs the same batch size on every rank.
 
 A layer is row-sharded when its output count divides evenly by the world size
 (at least 8 rows per rank); other layers all-reduce their dW and step every row
@@ -32,28 +45,36 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
+from . import _native as nat
 from . import _ops
 
 _ACTIVE = False
 _GROUP = None  # large transfers (dW, weights)
 _SMALL = None  # scalar / small-vector collectives
+_ACT = None  # activation all-gathers and dY all-to-all ("gather" exchange)
+_EXCHANGE = "reduce"
 _PENDING: list = []  # layers whose dW reduction is in flight
 COMM_SMS = 16  # SMs the GEMMs leave free for NCCL while data parallelism is active
 
 
-def init(group=None, comm_sms: int = COMM_SMS) -> None:
+def init(group=None, comm_sms: int = COMM_SMS, dw_exchange: str = "reduce") -> None:
     """Enable the exchanges on ``group`` (default: the world).  Collective: call on every rank.
 
     ``comm_sms``: SMs the persistent GEMMs leave to NCCL, so the dW
     reduce-scatter and the weight all-gather overlap the GEMMs instead of
-    waiting for them to finish.
+    waiting for them to finish.  ``dw_exchange``: ``"reduce"`` or ``"gather"``
+    (module docstring).
     """
-    global _ACTIVE, _GROUP, _SMALL
+    global _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE
     if not dist.is_initialized():
         raise RuntimeError("ecoint8.parallel.init needs torch.distributed to be initialized")
+    if dw_exchange not in ("reduce", "gather"):
+        raise ValueError(f"dw_exchange must be 'reduce' or 'gather', got {dw_exchange!r}")
     _GROUP = group
     ranks = list(range(dist.get_world_size())) if group is None else dist.get_process_group_ranks(group)
     _SMALL = dist.new_group(ranks=ranks)
+    _ACT = dist.new_group(ranks=ranks) if dw_exchange == "gather" else None
+    _EXCHANGE = dw_exchange
     _ACTIVE = True
     if torch.cuda.is_available() and comm_sms > 0 and len(ranks) > 1:
         from . import _native
@@ -63,9 +84,9 @@ def init(group=None, comm_sms: int = COMM_SMS) -> None:
 
 
 def shutdown() -> None:
-    global _ACTIVE, _GROUP, _SMALL
+    global _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE
     finalize_pending()
-    _ACTIVE, _GROUP, _SMALL = False, None, None
+    _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE = False, None, None, None, "reduce"
     if torch.cuda.is_available():
         from . import _native
 
@@ -77,6 +98,10 @@ def shutdown() -> None:
 
 def active() -> bool:
     return _ACTIVE and dist.is_initialized() and dist.get_world_size(_GROUP) > 1
+
+
+def exchange() -> str:
+    return _EXCHANGE
 
 
 def world() -> int:
@@ -130,14 +155,85 @@ def start_dw_reduction(layer, dw_acc: torch.Tensor, gb_sum: torch.Tensor, s_g: f
         lo, hi = rows
         red = torch.empty((hi - lo, dw_acc.shape[1]), dtype=dw_acc.dtype, device=dw_acc.device)
         work = dist.reduce_scatter_tensor(red, dw_acc, op=dist.ReduceOp.SUM, group=_GROUP, async_op=True)
-    layer._dw_pending = {"red": red, "full": dw_acc, "work": work, "gb": gb_sum, "rows": rows, "s_g": float(s_g)}
+    layer._dw_pending = {"red": red, "full": dw_acc, "shape": tuple(dw_acc.shape), "work": work, "gb": gb_sum,
+                         "rows": rows, "s_g": float(s_g)}
     _PENDING.append(layer)
 
 
-def global_max_dx(amax_dx: torch.Tensor) -> int:
-    t = amax_dx.reshape(1).to(torch.int64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_SMALL)
+# -- "gather" exchange ---------------------------------------------------------------
+def gathers_input(layer) -> bool:
+    """Whether ``layer``'s forward all-gathers its input (the "gather" exchange on a row-sharded layer)."""
+    return active() and _EXCHANGE == "gather" and shard_rows(layer.out_features) is not None
+
+
+def gather_input(layer, x_i8: torch.Tensor) -> None:
+    """Start the all-gather of a layer's int8 input over the global batch (rank-major rows)."""
+    x = x_i8.contiguous()
+    full = torch.empty((world() * x.shape[0], x.shape[1]), dtype=x.dtype, device=x.device)
+    work = dist.all_gather_into_tensor(full, x, group=_ACT, async_op=True)
+    layer._input_gather = (full, work)
+
+
+def column_blocks(g_i8: torch.Tensor) -> torch.Tensor:
+    """``[b, out]`` -> ``[world, b, out / world]``: column block s as one contiguous block (CUDA)."""
+    n = world()
+    b, out = g_i8.shape
+    c = out // n
+    g = _ops._rowmajor(g_i8)
+    nat.require_cuda(g)
+    send = torch.empty((n, b, c), dtype=g.dtype, device=g.device)
+    nat.call("eco_split_cols_s8", g.data_ptr(), g.stride(0) if b > 1 else out, b, out, n, send.data_ptr(),
+             nat.stream())
+    return send
+
+
+def exchange_blocks(send: torch.Tensor):
+    """All-to-all of ``column_blocks``: block s goes to rank s.  Returns the
+    ``[world * b, c]`` columns of this rank over the global batch (rows in the
+    order of ``gather_input``) and the work handle."""
+    n, b, c = send.shape
+    recv = torch.empty_like(send)
+    work = dist.all_to_all_single(recv, send, group=_ACT, async_op=True)
+    return recv.view(n * b, c), work
+
+
+def exchange_grad_columns(g_i8: torch.Tensor):
+    """Start the all-to-all that gives each rank its dY columns over the global batch."""
+    return exchange_blocks(column_blocks(g_i8))
+
+
+def start_dw_rows(layer, dy_cols: torch.Tensor, a2a, s_g: float) -> None:
+    """This rank's rows of the summed dW in one GEMM over the global batch ("gather" exchange)."""
+    full, xwork = layer._input_gather
+    layer._input_gather = None
+    a2a.wait()
+    xwork.wait()
+    out = layer.out_features
+    lo, hi = shard_rows(out)
+    K, in_f = full.shape
+    amax = torch.empty(1, dtype=torch.int32, device=full.device)
+    red = _ops.gemm_s32(dy_cols, 1, full, 1, hi - lo, in_f, K, amax=amax)
+    gb = torch.zeros(out, dtype=torch.int64, device=red.device)
+    gb[lo:hi] = _ops.colsum(dy_cols)  # the other rows arrive through the flat SUM in finalize_pending
+    layer._dw_pending = {"red": red, "full": None, "shape": (out, in_f), "work": None, "gb": gb,
+                         "rows": (lo, hi), "s_g": float(s_g), "amax": amax}
+    _PENDING.append(layer)
+
+
+def start_max(amax: torch.Tensor):
+    """Start the MAX over ranks of a device maximum; ``finish_max`` reads it."""
+    t = amax.reshape(1).to(torch.int64)
+    return t, dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_SMALL, async_op=True)
+
+
+def finish_max(handle) -> int:
+    t, work = handle
+    work.wait()
     return int(t.item())
+
+
+def global_max_dx(amax_dx: torch.Tensor) -> int:
+    return finish_max(start_max(amax_dx))
 
 
 def finalize_pending() -> None:
@@ -155,9 +251,16 @@ def finalize_pending() -> None:
         l._dw_pending["gb"] = flat[off:off + g.numel()]
         off += g.numel()
     for layer in layers:
-        layer._dw_pending["work"].wait()
+        if layer._dw_pending["work"] is not None:
+            layer._dw_pending["work"].wait()
     dev = layers[0].w_i8.device
-    maxima = torch.cat([_ops.amax(l._dw_pending["red"]).reshape(1) for l in layers])
+    # max|dW| of this rank's rows: the gather exchange's GEMM produced it already
+    fused = [l._dw_pending.get("amax") for l in layers]
+    if all(a is not None for a in fused):
+        maxima = torch.cat(fused).to(torch.int64)
+    else:
+        maxima = torch.cat([a.to(torch.int64) if a is not None else _ops.amax(l._dw_pending["red"]).reshape(1)
+                            for l, a in zip(layers, fused)])
     dist.all_reduce(maxima, op=dist.ReduceOp.MAX, group=_SMALL)
     sumsq = torch.zeros(len(layers), dtype=torch.int64, device=dev)
     for i, (layer, a_dw) in enumerate(zip(layers, maxima.tolist())):
@@ -179,14 +282,16 @@ def combine_step_state(state: torch.Tensor) -> None:
     state[:, 1:3].copy_(part)
 
 
-def gather_rows(layer, rowsum: torch.Tensor, rows) -> None:
-    """All-gather this rank's updated rows of w, b_acc and the row sums (asynchronous)."""
-    works = [dist.all_gather_into_tensor(layer.w_i8, layer.w_i8[rows[0]:rows[1]], group=_GROUP, async_op=True),
-             dist.all_gather_into_tensor(rowsum, rowsum[rows[0]:rows[1]], group=_GROUP, async_op=True)]
-    if layer.use_bias:
-        works.append(dist.all_gather_into_tensor(layer.b_acc, layer.b_acc[rows[0]:rows[1]], group=_GROUP,
-                                                 async_op=True))
-    layer._gather_works = works
+def gather_rows(layer, rows) -> None:
+    """All-gather this rank's updated weight rows (asynchronous; the biases are
+    stepped in full on every rank)."""
+    layer._gather_works = [dist.all_gather_into_tensor(layer.w_i8, layer.w_i8[rows[0]:rows[1]], group=_GROUP,
+                                                       async_op=True)]
+
+
+def gather_flat(flat: torch.Tensor):
+    """All-gather a rank-major ``[world, k]`` buffer whose row ``rank()`` this rank filled."""
+    return dist.all_gather_into_tensor(flat, flat[rank()], group=_SMALL, async_op=True)
 
 
 def wait_gathers(layer) -> None:

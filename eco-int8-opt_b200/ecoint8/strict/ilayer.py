@@ -7,11 +7,12 @@ tensor work runs on the B200 library:
   per-channel (mult, shift) requant, stochastic rounding, int8 saturation and
   -- when ``I8Sequential`` sees an ``I8ReLU`` next -- the ReLU in its
   epilogue.  The int32 accumulator never reaches HBM.
-* ``backward_i8`` runs the dW and dX GEMMs with a fused max|acc|, reads both
-  maxima with one device->host copy (the reference reads them one by one),
-  then one requant kernel each; the dW requant also produces the square sum
-  that ``I8ECO``'s gradient clip needs, and the dX requant applies the mask of
-  the preceding ``I8ReLU``.
+* ``backward_i8`` runs the dX and dW GEMMs with a fused max|acc|, then one
+  requant kernel each; the maxima come back on a side stream, so the host
+  reads the dX maximum while the dW GEMM runs and the device never waits for
+  the host; the dW requant also produces the square sum that ``I8ECO``'s
+  gradient clip needs, and the dX requant applies the mask of the preceding
+  ``I8ReLU``.
 * Scales stay plain Python floats computed by the reference's expressions, so
   every multiplier and shift is bit-identical.
 
@@ -49,6 +50,23 @@ class _ScaleList(list):
         # unpickling appends the items before it restores __dict__
         self.version = getattr(self, "version", 0) + 1
 
+    def _before_edit(self):
+        snap = self.__dict__.pop("_snap", None)
+        if snap is not None:  # an outstanding snapshot keeps the values it was taken with
+            snap[0] = list(self)
+
+    def snapshot(self):
+        """The current values, copied only if the list is edited before ``values(token)``."""
+        snap = self.__dict__.get("_snap")
+        if snap is None:
+            snap = self.__dict__["_snap"] = [None]
+        return self, snap
+
+    @staticmethod
+    def values(token) -> list:
+        lst, snap = token
+        return lst if snap[0] is None else snap[0]
+
 
 for _name in ("__setitem__", "__delitem__", "__iadd__", "__imul__", "append", "extend", "insert", "pop",
               "remove", "clear", "sort", "reverse"):
@@ -56,6 +74,7 @@ for _name in ("__setitem__", "__delitem__", "__iadd__", "__imul__", "append", "e
         base = getattr(list, name)
 
         def method(self, *a, **k):
+            self._before_edit()
             r = base(self, *a, **k)
             self._edited()
             return self if name in ("__iadd__", "__imul__") else r
@@ -134,6 +153,18 @@ class I8Linear(nn.Module):
         self._dw_pending = None
         self._fwd_cache = None
         self._sw_cache = None
+
+    # Per-call bookkeeping attributes bypass nn.Module.__setattr__ (none is a
+    # parameter, buffer or submodule; properties still apply).
+    _PLAIN_ATTRS = frozenset({"_cache_x", "_dw_pending", "_fwd_cache", "_gb_s", "_gb_sum", "_gw_rows", "_gw_s",
+                              "_gw_i8", "_gw_sumsq", "_gw_sumsq_of", "_sw_cache", "_input_gather",
+                              "_gather_works"})
+
+    def __setattr__(self, name, value):
+        if name in I8Linear._PLAIN_ATTRS:
+            object.__setattr__(self, name, value)
+        else:
+            super().__setattr__(name, value)
 
     # Gradient stashes of the reference (ilayer.py:155-156, 168-169).  Under data
     # parallelism the dW reduction is still in flight when backward_i8 returns;
@@ -228,6 +259,8 @@ class I8Linear(nn.Module):
         _native.require_cuda(x_i8, self.w_i8)
         assert isinstance(self.sx, float) and isinstance(self.sy, float)
         parallel.wait_gathers(self)
+        if parallel.gathers_input(self):
+            parallel.gather_input(self, x_i8)  # the global-batch input of this layer's dW ("gather" exchange)
         mults, com = self._fwd_mults(x_i8.device)
         N, K = x_i8.shape
         out = self.out_features
@@ -253,56 +286,75 @@ class I8Linear(nn.Module):
         if parallel.active():
             return self._backward_dp(g_i8, float(s_g), x_i8, _mask, dev)
         amax = torch.empty(2, dtype=torch.int32, device=dev)
-        # dW = g^T x: A = g stored [K=N, M=out], B = x stored [K=N, N=in]
-        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N, amax=amax[0:1])
+        # dX first: its maximum gates the next layer, and the host reads it while the dW GEMM runs
         # dX = g w: A = g [M=N, K=out], B = w stored [K=out, N=in]
         dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax[1:2])
-        gb_sum = _ops.colsum(g_i8)
-        key_w = _sr.reserve_key()  # the dW site's key (data-parallel runs take it at this point too)
-        a_dw, a_dx = amax.tolist()  # the one host synchronisation of this layer
-        # dW: exact scales (both per-tensor) -> int8 grad for the optimizer
-        s_gw = dynamic_scale_from_int(a_dw, s_g * s_x)
-        m_gw, sh_gw = quantize_multiplier((s_g * s_x) / s_gw)
-        if key_w is not None:
-            _check_shift(sh_gw, True)
-            site = _sr.site_from_key(key_w, (out, in_f), sh_gw, 0, "dw")
-        else:
-            site = _requant_site((out, in_f), sh_gw, dev, False, "dw")
-        self._gw_sumsq = torch.empty(1, dtype=torch.int64, device=dev)
-        self._gw_i8 = _ops.requant(dw_acc, m_gw, sh_gw, site, sumsq=self._gw_sumsq)
-        self._gw_sumsq_of = self._gw_i8
-        self._gw_s = s_gw
-        self._gw_rows = None
-        # dX: per-channel s_w approximated by its mean
-        sw_mean = self._sw_mean()
-        s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
-        m_dx, sh_dx = quantize_multiplier((s_g * sw_mean) / s_dx)
-        site = _requant_site((N, in_f), sh_dx, dev, True, "dx")
-        dx_i8 = _ops.requant(dx_acc, m_dx, sh_dx, site, mask=_mask)
-        # dBias: integer column sums of g_i8 (torch's int32 .sum(0) returns int64)
-        self._gb_sum = gb_sum
+        rd_dx = _ops.read_later(amax[1:2])
+        # dW = g^T x: A = g stored [K=N, M=out], B = x stored [K=N, N=in]
+        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N, amax=amax[0:1])
+        rd_dw = _ops.read_later(amax[0:1])
+        self._gb_sum = _ops.colsum(g_i8)  # dBias: integer column sums (torch's int32 .sum(0) is int64)
         self._gb_s = float(s_g)
+        key_w = _sr.reserve_key()  # the dW site's key, in the reference's draw order
+
+        def requant_dw(a_dw):
+            # dW: exact scales (both per-tensor) -> int8 grad for the optimizer
+            s_gw = dynamic_scale_from_int(a_dw, s_g * s_x)
+            m_gw, sh_gw = quantize_multiplier((s_g * s_x) / s_gw)
+            if key_w is not None:
+                _check_shift(sh_gw, True)
+                site = _sr.site_from_key(key_w, (out, in_f), sh_gw, 0, "dw")
+            else:
+                site = _requant_site((out, in_f), sh_gw, dev, False, "dw")
+            self._gw_sumsq = torch.empty(1, dtype=torch.int64, device=dev)
+            self._gw_i8 = _ops.requant(dw_acc, m_gw, sh_gw, site, sumsq=self._gw_sumsq)
+            self._gw_sumsq_of = self._gw_i8
+            self._gw_s = s_gw
+            self._gw_rows = None
+
+        def requant_dx(a_dx):
+            # dX: per-channel s_w approximated by its mean
+            sw_mean = self._sw_mean()
+            s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
+            m_dx, sh_dx = quantize_multiplier((s_g * sw_mean) / s_dx)
+            site = _requant_site((N, in_f), sh_dx, dev, True, "dx")
+            return _ops.requant(dx_acc, m_dx, sh_dx, site, mask=_mask), s_dx
+
+        if key_w is None:  # replay: the dW site draws first, and its draw needs the dW shift
+            requant_dw(rd_dw.value()[0])
+            return requant_dx(rd_dx.value()[0])
+        dx_i8, s_dx = requant_dx(rd_dx.value()[0])  # queued behind the dW GEMM: no idle gap
+        requant_dw(rd_dw.value()[0])
         return dx_i8, s_dx
 
-
     def _backward_dp(self, g_i8, s_g, x_i8, mask, dev):
-        """Data-parallel backward: asynchronous row reduce-scatter of dW (finalized when the
-        gradient is read), global dX maximum over ranks, dX requant.  Same draws and
-        results as the single-device backward on the concatenated batch."""
+        """Data-parallel backward: dW rows formed asynchronously (reduce-scatter of the
+        int32 accumulators, or one GEMM over the gathered global batch) and finalized
+        when the gradient is read; global dX maximum over ranks; dX requant.  Same
+        draws and results as the single-device backward on the concatenated batch."""
         N, out = g_i8.shape
         in_f = x_i8.shape[1]
-        s_x = self.sx
-        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N)
-        gb_sum = _ops.colsum(g_i8)
+        gathered = self.__dict__.get("_input_gather") is not None
+        if gathered:
+            dy_cols, a2a = parallel.exchange_grad_columns(g_i8)
+        else:
+            dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N)
+            gb_sum = _ops.colsum(g_i8)
         key_w = _sr.reserve_key()  # the dW site's key, in the reference's draw order
-        parallel.start_dw_reduction(self, dw_acc, gb_sum, s_g)
-        self._dw_pending["key"] = key_w
+        if not gathered:
+            parallel.start_dw_reduction(self, dw_acc, gb_sum, s_g)
+            self._dw_pending["key"] = key_w
         self._gb_s = float(s_g)
-        if key_w is None:  # replay mode draws in order: finish this layer's dW now
-            parallel.finalize_pending()
         amax_dx = torch.empty(1, dtype=torch.int32, device=dev)
         dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax_dx)
-        a_dx = parallel.global_max_dx(amax_dx)
+        t, work = parallel.start_max(amax_dx)
+        rd_dx = _ops.read_later(t, work)
+        if gathered:  # the dW GEMM runs while the host waits for the dX maximum
+            parallel.start_dw_rows(self, dy_cols, a2a, s_g)
+            self._dw_pending["key"] = key_w
+        if key_w is None:  # replay mode draws in order: finish this layer's dW now
+            parallel.finalize_pending()
+        a_dx = rd_dx.value()[0]
         sw_mean = self._sw_mean()
         s_dx = dynamic_scale_from_int(a_dx, s_g * sw_mean)
         m_dx, sh_dx = quantize_multiplier((s_g * sw_mean) / s_dx)
@@ -315,7 +367,7 @@ class I8Linear(nn.Module):
         p = self.__dict__["_dw_pending"]
         self._dw_pending = None
         s_g, s_x = p["s_g"], self.sx
-        out, in_f = p["full"].shape
+        out, in_f = p["shape"]
         s_gw = dynamic_scale_from_int(a_dw, s_g * s_x)
         m_gw, sh_gw = quantize_multiplier((s_g * s_x) / s_gw)
         _check_shift(sh_gw, True)
@@ -340,6 +392,12 @@ class I8ReLU(nn.Module):
     Inside ``I8Sequential`` the clamp runs in the preceding layer's GEMM
     epilogue and the mask is its output's sign, materialised only if read.
     """
+
+    def __setattr__(self, name, value):
+        if name in ("_mask", "_relu_out"):  # bookkeeping, not parameters or buffers
+            object.__setattr__(self, name, value)
+        else:
+            super().__setattr__(name, value)
 
     def __init__(self):
         super().__init__()

@@ -37,6 +37,9 @@ import torch
 from .. import _native as nat
 from .. import _ops, _sr, parallel
 from ..fixedpoint import _check_int, quantize_multiplier
+from .ilayer import _ScaleList
+
+layer_values = _ScaleList.values
 
 __all__ = ["I8ECO"]
 
@@ -120,10 +123,15 @@ class I8ECO:
     @property
     def stats(self) -> dict:
         if self._pending_stats is not None:
-            parallel.synchronize(self.layers)  # row sums of other ranks (data parallel)
+            work = getattr(self, "_rowsum_work", None)
+            if work is not None:  # row sums of other ranks (data parallel)
+                work.wait()
+                self._rowsum_work = None
             self._raise_pending(block=True)
             tot_e, n_e = 0.0, 0
-            for rowsum, sw, rowlen, out in self._pending_stats:
+            for src, token, rowlen, out in self._pending_stats:
+                sw = layer_values(token)
+                rowsum = src if isinstance(src, torch.Tensor) else src[0][:, src[1]:src[1] + src[2]].reshape(-1)
                 rs = rowsum.tolist()
                 tot_e += sum(s * sw_o for s, sw_o in zip(rs, sw)) / rowlen / (1 << FRAC_BITS)  # iopt.py:183
                 n_e += out
@@ -195,57 +203,36 @@ class I8ECO:
         replay = _sr.replaying()
         if replay:
             s_m_now = [_float(v) for v in self._state[:, 0].tolist()]
-        keep = []  # tensors that must outlive the launch
-        descs = []
-        pending = []
-        sharded = []  # (layer, rowsum, rows) stepped on this rank's rows only
         dp = parallel.active()
-        for i, layer in active:
-            g_i8 = layer._gw_i8
-            _check_int(g_i8, "weight grad")
+        plan = self._plan(active, dev, dp)
+        keep = []  # tensors that must outlive the launch
+        for (i, layer), d, rows in zip(active, plan["descs"], plan["rows"]):
+            g = layer._gw_i8
+            _check_int(g, "weight grad")
             w = layer.w_i8
-            if self.m_i8[i].device != w.device:  # layer moved after construction: follow it
-                self.m_i8[i] = self.m_i8[i].to(w.device)
-            m = self.m_i8[i]
-            nat.require_cuda(g_i8, w, m)
-            g = g_i8.contiguous()
-            rows = getattr(layer, "_gw_rows", None)  # this rank's row shard under data parallelism
             lo, hi = (0, w.shape[0]) if rows is None else rows
-            if (g.dtype != torch.int8 or not (w.is_contiguous() and m.is_contiguous())
-                    or tuple(g.shape) != (hi - lo, w.shape[1])):
+            if g.dtype != torch.int8 or not g.is_contiguous() or tuple(g.shape) != (hi - lo, w.shape[1]):
                 raise RuntimeError("I8ECO: weights, momentum and gradient must be contiguous int8 of one shape")
+            nat.require_cuda(g)
             out, rowlen = w.shape
             s_g = float(layer._gw_s)
-            sw_bits, sw_min, sw_max = layer._sw_device(dev)
             gsq = self._gsq(layer, g) if self.grad_clip is not None else None
-            if self._rowsum[i] is None or self._rowsum[i].numel() != out or self._rowsum[i].device != dev:
-                self._rowsum[i] = torch.empty(out, dtype=torch.int64, device=dev)
-            d = nat.I8ECOLayer()
-            d.w, d.m, d.g = w.data_ptr() + lo * rowlen, m.data_ptr() + lo * rowlen, g.data_ptr()
-            d.sw = sw_bits.data_ptr() + 8 * lo
-            d.rowsum, d.gsq = self._rowsum[i].data_ptr() + 8 * lo, nat.ptr(gsq)
-            d.state = self._state[i].data_ptr()
-            d.rows, d.cols, d.row_base = hi - lo, rowlen, lo
-            d.sw_min, d.sw_max, d.s_g = sw_min, sw_max, s_g
-            d.stream_w, d.stream_b = 2 * i, 2 * i + 1
+            d.g, d.gsq, d.s_g = g.data_ptr(), nat.ptr(gsq), s_g
+            d.nudge_w = d.nudge_m = d.nudge_b = None
             d.nudge_m_bits = d.nudge_b_bits = 32
             if layer.use_bias:
-                assert isinstance(layer.sx, float)
-                gb = layer._gb_sum.to(device=dev, dtype=torch.int64).contiguous()
+                gb = layer._gb_sum
+                if gb.dtype != torch.int64 or gb.device != dev or not gb.is_contiguous():
+                    gb = gb.to(device=dev, dtype=torch.int64).contiguous()
                 s_gb = float(layer._gb_s)
-                com_b = _common_shift([self.lr * s_gb / (layer.sx * sw_min)])  # = min over rows
+                com_b = _common_shift([self.lr * s_gb / (layer.sx * d.sw_min)])  # = min over rows
                 if com_b > 62:  # the reference's torch.randint(0, 2**com_b) raises (iopt.py:194)
                     raise ValueError("Overflow when unpacking long long")
-                d.b_acc, d.gb_sum = layer.b_acc.data_ptr() + 4 * lo, gb.data_ptr() + 8 * lo
-                d.s_gb, d.sx = s_gb, layer.sx
+                d.gb_sum, d.s_gb = gb.data_ptr() + 8 * lo, s_gb
                 keep.append(gb)
             if replay:
                 keep += self._replay_nudges(d, layer, s_m_now[i], s_g, gsq, (out, rowlen), lo)
-            keep += [g, gsq, sw_bits]
-            descs.append(d)
-            pending.append((self._rowsum[i], list(layer.sw), rowlen, out))
-            if rows is not None:
-                sharded.append((layer, self._rowsum[i], rows))
+            keep += [g, gsq]
         hyper = nat.I8ECOHyper()
         hyper.lr = self.lr
         hyper.grad_clip = -1.0 if self.grad_clip is None else float(self.grad_clip)
@@ -256,14 +243,19 @@ class I8ECO:
         hyper.done_counter = self._counter.data_ptr()
         if _sr.LOG is not None and not replay:
             _sr.LOG.append(("i8eco_step", hyper.seed, [(i, 2 * i, 2 * i + 1) for i, _ in active]))
-        arr = (nat.I8ECOLayer * len(descs))(*descs)
-        nat.call("eco_i8eco_step", arr, len(descs), ctypes.byref(hyper), nat.stream())
+        self._keep_plan = plan
+        nat.call("eco_i8eco_step", plan["arr"], len(active), ctypes.byref(hyper), nat.stream())
+        self._rowsum_work = None
         if dp:
             parallel.combine_step_state(self._state)
             nat.call("eco_i8eco_finalize", self._state.data_ptr(), self._state.shape[0], nat.stream())
-            for layer, rowsum, rows in sharded:
-                parallel.gather_rows(layer, rowsum, rows)
-        self._pending_stats = pending
+            for (_, layer), rows in zip(active, plan["rows"]):
+                if rows is not None:
+                    parallel.gather_rows(layer, rows)
+            if plan["flat"] is not None:
+                self._rowsum_work = parallel.gather_flat(plan["flat"])
+        self._pending_stats = [(src, layer.sw.snapshot(), layer.w_i8.shape[1], layer.out_features)
+                               for (_, layer), src in zip(active, plan["rowsum"])]
         # error flags come back asynchronously into one of two persistent pinned buffers
         # (allocating pinned memory every step can stall the host)
         if getattr(self, "_flag_bufs", None) is None or self._flag_bufs[0][0].numel() != len(self.layers):
@@ -277,6 +269,67 @@ class I8ECO:
         ev.record()
         self._err = (ev, flags)
         self._keep = keep  # released at the next step (stream-ordered reuse is safe)
+
+    def _plan(self, active, dev, dp):
+        """The step's layer descriptors with every field that does not change between
+        steps filled in; rebuilt only when a layer, its storage, its row shard or its
+        scales change.  Under data parallelism the row sums of the sharded layers live
+        in one rank-major ``[world, sum of shard rows]`` buffer (one all-gather)."""
+        world = parallel.world() if dp else 1
+        rank = parallel.rank() if dp else 0
+        key = [dp, world, rank, str(dev), self._state.data_ptr()]
+        for i, layer in active:
+            if self.m_i8[i].device != layer.w_i8.device:  # layer moved after construction: follow it
+                self.m_i8[i] = self.m_i8[i].to(layer.w_i8.device)
+            key.append((i, id(layer), layer.w_i8.data_ptr(), tuple(layer.w_i8.shape), self.m_i8[i].data_ptr(),
+                        getattr(layer, "_gw_rows", None), layer.use_bias,
+                        layer.b_acc.data_ptr() if layer.use_bias else 0, layer._sw_key(), layer.sx))
+        plan = getattr(self, "_plan_cache", None)
+        if plan is not None and plan["key"] == key:
+            return plan
+        shard_total = sum(r[1] - r[0] for r in (getattr(l, "_gw_rows", None) for _, l in active) if r is not None)
+        flat = torch.empty((world, shard_total), dtype=torch.int64, device=dev) if dp and shard_total else None
+        descs, rows_l, rowsum_l = [], [], []
+        off = 0
+        for i, layer in active:
+            w, m = layer.w_i8, self.m_i8[i]
+            nat.require_cuda(w, m)
+            if not (w.dtype == torch.int8 and m.dtype == torch.int8 and w.is_contiguous() and m.is_contiguous()
+                    and m.shape == w.shape):
+                raise RuntimeError("I8ECO: weights, momentum and gradient must be contiguous int8 of one shape")
+            rows = getattr(layer, "_gw_rows", None)  # this rank's row shard under data parallelism
+            lo, hi = (0, w.shape[0]) if rows is None else rows
+            out, rowlen = w.shape
+            sw_bits, sw_min, sw_max = layer._sw_device(dev)
+            d = nat.I8ECOLayer()
+            d.w, d.m = w.data_ptr() + lo * rowlen, m.data_ptr() + lo * rowlen
+            d.sw = sw_bits.data_ptr() + 8 * lo
+            if rows is not None and flat is not None:
+                d.rowsum = flat[rank, off:off + hi - lo].data_ptr()
+                rowsum_l.append((flat, off, hi - lo))
+                off += hi - lo
+            else:
+                if self._rowsum[i] is None or self._rowsum[i].numel() != out or self._rowsum[i].device != dev:
+                    self._rowsum[i] = torch.empty(out, dtype=torch.int64, device=dev)
+                d.rowsum = self._rowsum[i].data_ptr()
+                rowsum_l.append(self._rowsum[i])
+            d.state = self._state[i].data_ptr()
+            d.rows, d.cols, d.row_base = hi - lo, rowlen, lo
+            d.sw_min, d.sw_max = sw_min, sw_max
+            d.stream_w, d.stream_b = 2 * i, 2 * i + 1
+            d.bias_rows = 0
+            if layer.use_bias:
+                assert isinstance(layer.sx, float)
+                d.b_acc, d.sx = layer.b_acc.data_ptr() + 4 * lo, layer.sx
+                if rows is not None:  # every rank steps every bias (gb_sum is complete on each rank)
+                    d.bias_rows = out
+            descs.append(d)
+            rows_l.append(rows)
+        arr = (nat.I8ECOLayer * len(descs))(*descs)
+        plan = {"key": key, "arr": arr, "descs": list(arr), "rows": rows_l, "rowsum": rowsum_l, "flat": flat,
+                "sw": [layer._sw_device(dev)[0] for _, layer in active]}
+        self._plan_cache = plan
+        return plan
 
     def _replay_nudges(self, d, layer, s_m: float, s_g: float, gsq, shape, lo: int = 0):
         """Verification mode: draw in the reference's order (iopt.py:152-197), consume whole.

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define ECO_ABI_VERSION 1
+#define ECO_ABI_VERSION 2
 
 enum {
   ECO_OK = 0,
@@ -148,6 +148,14 @@ ECO_API int eco_read_device_errors(uint32_t* flags);
 ECO_API int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_t ld_dst, int64_t rows,
                   int64_t cols, eco_stream_t stream);
 
+/* Splits the columns of a [rows, cols] int8 matrix into `parts` equal blocks and
+ * stores block p as a contiguous [rows, cols / parts] matrix at dst + p * rows *
+ * (cols / parts): the send buffer of the data-parallel all-to-all that hands
+ * each rank its dY columns.  No reference counterpart (the reference has no
+ * data parallelism). */
+ECO_API int eco_split_cols_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int64_t parts,
+                      int8_t* dst, eco_stream_t stream);
+
 /* -------------------------------------------------------- I8ECO step -----
  * One fused, single-pass integer ECO-SGDM step over a list of layers
  * (ecoint8/strict/iopt.py:103-200): per-row fixed-point multipliers and common
@@ -180,6 +188,12 @@ typedef struct {
   uint64_t stream_b;      /* Philox site of the bias nudges */
   int32_t nudge_m_bits;   /* 32 or 64 */
   int32_t nudge_b_bits;   /* 32 or 64 */
+  int64_t bias_rows;      /* 0: the bias of the stepped rows.  > 0: the bias of the layer's
+                             global rows [0, bias_rows) instead, with b_acc, gb_sum, sw and
+                             nudge_b indexed by (global row - row_base), so they must cover
+                             those rows: a data-parallel row shard then updates every bias
+                             (the bias step does not depend on the weights) and no rank has
+                             to receive the others' biases */
 } eco_i8eco_layer_t;
 
 typedef struct {

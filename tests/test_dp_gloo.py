@@ -68,3 +68,51 @@ def test_two_rank_backward_exchange_is_exact():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert sorted(res) == [(0, True), (1, True)]
+
+
+def _gather_worker(rank, world, port, q):
+    """The "gather" exchange: all-gathered inputs and all-to-all dY columns give each
+    rank exactly its rows of the full-batch dW and of the bias sums."""
+    import types
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    try:
+        from ecoint8 import parallel
+
+        parallel.init(dw_exchange="gather")
+        gen = torch.Generator().manual_seed(5)
+        b, out, inn = 16, 8 * world, 20
+        g = torch.randint(-127, 128, (b * world, out), dtype=torch.int8, generator=gen)
+        x = torch.randint(-127, 128, (b * world, inn), dtype=torch.int8, generator=gen)
+        layer = types.SimpleNamespace(out_features=out)
+        ok = parallel.gathers_input(layer) and parallel.exchange() == "gather"
+        parallel.gather_input(layer, x[rank * b:(rank + 1) * b])
+        # the column blocks of this rank's dY (a CUDA copy in the library; built here on the CPU)
+        mine = g[rank * b:(rank + 1) * b]
+        dy_cols, a2a = parallel.exchange_blocks(mine.reshape(b, world, out // world).transpose(0, 1).contiguous())
+        full, work = layer._input_gather
+        a2a.wait()
+        work.wait()
+        lo, hi = parallel.shard_rows(out)
+        rows = ofp.int_mm(dy_cols.numpy().T, full.numpy())
+        ok &= np.array_equal(rows, ofp.int_mm(g.numpy().T, x.numpy())[lo:hi])
+        ok &= np.array_equal(dy_cols.numpy().astype(np.int64).sum(0), g.numpy()[:, lo:hi].astype(np.int64).sum(0))
+        q.put((rank, bool(ok)))
+        parallel.shutdown()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_three_rank_gather_exchange_gives_row_shards_of_full_dw():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert sorted(res) == [(0, True), (1, True), (2, True)]

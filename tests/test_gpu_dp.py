@@ -1,4 +1,5 @@
-"""Data parallelism on 2 GPUs reproduces the single-GPU run bit for bit (NCCL).
+"""Data parallelism on 2 GPUs reproduces the single-GPU run bit for bit (NCCL),
+with either dW exchange (int32 reduce-scatter, or gathered inputs + dY all-to-all).
 
 Two ranks split a batch of 96 rows; rank 0 also trains an identical net on the
 whole batch on its own.  Both use the same Philox key sequence, so after
@@ -89,22 +90,27 @@ def _worker(rank, port, q):
         Y = torch.randint(0, C, (B,), generator=gen)
         X8, sx = quantize_tensor_dynamic(X)  # entry scale of the global batch, identical on both ranks
         lo, hi = rank * B // 2, (rank + 1) * B // 2
-        parallel.init()
-        net = _net(dev)
-        opt = _train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), 2, lo, 123, 4)
-        parallel.synchronize(net.int8_layers())  # the last step's row all-gathers
-        parallel.gather_momentum(opt)  # momentum rows live on their owner rank
-        stats = opt.stats["mean_abs_e"]
-        parallel.shutdown()
+        runs = {}
+        for exchange in ("reduce", "gather"):
+            parallel.init(dw_exchange=exchange)
+            net = _net(dev)
+            opt = _train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), 2, lo, 123, 4)
+            parallel.synchronize(net.int8_layers())  # the last step's row all-gathers
+            parallel.gather_momentum(opt)  # momentum rows live on their owner rank
+            runs[exchange] = (net, opt, opt.stats["mean_abs_e"])
+            parallel.shutdown()
         if rank == 0:
             single = _net(dev)
             sopt = _train(single, X8.to(dev), sx, Y.to(dev), 1, 0, 123, 4)
-            ok = all(torch.equal(a.w_i8, b.w_i8) for a, b in zip(net.int8_layers(), single.int8_layers()))
-            ok &= all(torch.equal(a.b_acc, b.b_acc) for a, b in zip(net.int8_layers(), single.int8_layers()))
-            ok &= all(torch.equal(a, b) for a, b in zip(opt.m_i8, sopt.m_i8))
-            ok &= opt.s_m == sopt.s_m
-            ok &= stats == sopt.stats["mean_abs_e"]
-            q.put(bool(ok))
+            res = {}
+            for exchange, (net, opt, stats) in runs.items():
+                ok = all(torch.equal(a.w_i8, b.w_i8) for a, b in zip(net.int8_layers(), single.int8_layers()))
+                ok &= all(torch.equal(a.b_acc, b.b_acc) for a, b in zip(net.int8_layers(), single.int8_layers()))
+                ok &= all(torch.equal(a, b) for a, b in zip(opt.m_i8, sopt.m_i8))
+                ok &= opt.s_m == sopt.s_m
+                ok &= stats == sopt.stats["mean_abs_e"]
+                res[exchange] = bool(ok)
+            q.put(res)
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -129,4 +135,4 @@ def test_two_gpu_data_parallel_equals_single_gpu():
     for p in ps:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert ok
+    assert ok == {"reduce": True, "gather": True}

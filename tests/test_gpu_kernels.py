@@ -158,6 +158,20 @@ def test_reductions_colsum_amax_sumsq():
         assert int(_ops.amax(x.cuda()).item()) == int(x.to(torch.int64).abs().max())
 
 
+def test_split_cols_matches_block_transpose():
+    """eco_split_cols_s8 (the all-to-all send layout) equals the reshaped transpose."""
+    from ecoint8 import _native
+
+    gen = torch.Generator().manual_seed(3)
+    for rows, cols, parts, ld in [(48, 48, 2, 48), (2048, 8192, 8, 8192), (7, 30, 3, 33), (5, 1000, 8, 1000)]:
+        full = torch.randint(-127, 128, (rows, ld), dtype=torch.int8, generator=gen).cuda()
+        src = full[:, :cols]
+        dst = torch.empty((parts, rows, cols // parts), dtype=torch.int8, device="cuda")
+        _native.call("eco_split_cols_s8", src.data_ptr(), ld, rows, cols, parts, dst.data_ptr(), _native.stream())
+        want = src.reshape(rows, parts, cols // parts).transpose(0, 1)
+        assert torch.equal(dst, want), (rows, cols, parts)
+
+
 def test_library_reports_no_device_timeouts():
     from ecoint8 import _native
 

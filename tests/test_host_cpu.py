@@ -24,7 +24,7 @@ def test_library_loads_and_exports_every_header_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert sorted(names) == sorted(_native.exported_symbols())
-    assert lib.eco_abi_version() == 1
+    assert lib.eco_abi_version() == 2
 
 
 def test_c_abi_rejects_bad_arguments_with_a_message():
@@ -140,6 +140,13 @@ def test_weight_steps_track_edits_and_pickle():
     buf.seek(0)
     back = torch.load(buf, weights_only=False)
     assert back.sw == [1.0, 2.0, 3.0, 4.0] and torch.equal(back.w_i8, lin.w_i8)
+    # a statistics snapshot keeps the values it was taken with across later edits
+    tok = back.sw.snapshot()
+    assert type(back.sw).values(tok) == [1.0, 2.0, 3.0, 4.0]
+    back.sw[1] = 9.0
+    back.sw.append(5.0)
+    assert type(back.sw).values(tok) == [1.0, 2.0, 3.0, 4.0]
+    assert type(back.sw).values(back.sw.snapshot()) == [1.0, 9.0, 3.0, 4.0, 5.0]
 
 
 def test_replay_sites_follow_reference_order_without_gpu():
