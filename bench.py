@@ -327,9 +327,10 @@ def main():
     ap.add_argument("--only", choices=["gemm", "eco_step", "requant"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
-    ap.add_argument("--dw-exchange", default="gather", choices=["gather", "reduce"],
+    ap.add_argument("--dw-exchange", default="gather", choices=["gather", "reduce", "peer"],
                     help="how ranks form the summed dW rows (ecoint8.parallel.init)")
-    ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to NCCL under data parallelism")
+    ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to the exchange under data parallelism")
+    ap.add_argument("--push-ctas", type=int, default=16, help="CTAs per push kernel of the peer exchange")
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")
     args = ap.parse_args()
@@ -385,7 +386,7 @@ def main():
     from ecoint8._sr import batch_rows, set_generator
 
     if world > 1:
-        parallel.init(dw_exchange=args.dw_exchange, comm_sms=args.comm_sms)
+        parallel.init(dw_exchange=args.dw_exchange, comm_sms=args.comm_sms, push_ctas=args.push_ctas)
     set_generator(torch.Generator().manual_seed(1234))  # identical Philox keys on every rank
     local_b = GLOBAL_BATCH // world
     torch.manual_seed(0)
@@ -471,6 +472,7 @@ def main():
                           "global_batch": GLOBAL_BATCH, "per_gpu_batch": local_b, "parallelism": f"dp{world}",
                           "dw_exchange": args.dw_exchange if world > 1 else None,
                           "comm_sms": args.comm_sms if world > 1 else None,
+                          "push_ctas": args.push_ctas if world > 1 and args.dw_exchange == "peer" else None,
                           "l2": "inputs larger than L2 (1.2 GB activations + 0.55 GB weights); no flush"},
                "e2e": {"value": e2e, "unit": "steps/s", "h2d_bytes_per_step": int(x_i8.numel() + y.numel() * 8),
                        "d2h_bytes_per_step": 4},

@@ -518,12 +518,16 @@ extern "C" int eco_set_gemm_sm_limit(int max_ctas) {
   return ECO_OK;
 }
 
+int eco_peer_errors_take(unsigned* out);  // peer.cu
+
 extern "C" int eco_read_device_errors(uint32_t* flags) {
   ECO_REQUIRE(flags, ECO_ERR_ARG, "eco_read_device_errors: null output");
   unsigned v = 0, zero = 0;
   if (cudaMemcpyFromSymbol(&v, g_eco_device_errors, sizeof(v)) != cudaSuccess ||
       cudaMemcpyToSymbol(g_eco_device_errors, &zero, sizeof(zero)) != cudaSuccess)
     return eco_launch_check("eco_read_device_errors");
-  *flags = v;
+  unsigned peer = 0;
+  if (int rc = eco_peer_errors_take(&peer)) return rc;
+  *flags = v | peer;
   return ECO_OK;
 }

@@ -1,0 +1,184 @@
+// Data-parallel exchange over NVLink peer memory (one process per GPU).
+//
+// The buffers are allocated symmetrically on every rank and mapped into each
+// process; a rank reaches a peer's copy through that peer's pointer.  Pushes are
+// plain 16-byte stores into the peers' buffers (the SMs drive NVLink directly,
+// without the per-channel copy loop of a collective library), and completion is
+// published through per-rank flag words with release/acquire at system scope.
+// Every wait is bounded: on expiry it records ECO_FLAG_WAIT_TIMEOUT in a sticky
+// device word (read by eco_read_device_errors) and returns.
+#include "abi.cuh"
+#include "common.cuh"
+
+#include <algorithm>
+#include <type_traits>
+
+namespace {
+
+__device__ unsigned g_peer_errors;  // sticky flags of the bounded peer waits
+
+constexpr unsigned long long kPeerWaitNs = 5ull * 1000 * 1000 * 1000;  // 5 s
+
+struct PushArgs {
+  const int8_t* src;
+  int64_t ld_src, rows, cols;
+  int8_t* dst[ECO_MAX_PEERS];
+  int64_t ld_dst, dst_row0;
+  int n, split;
+};
+
+// Broadcast: every destination receives all of src at rows dst_row0 + r.
+// Split: destination p receives columns [p * c, (p + 1) * c), c = cols / n.
+// A block copies kRows rows at a time (rows blockIdx.x + i * gridDim.x), each
+// thread one unit of every row: all kRows loads are in flight before the stores,
+// so a few CTAs keep enough bytes moving to fill NVLink.  VEC: 16-byte units
+// (cols, c, ld_src, ld_dst multiples of 16 and aligned bases), else bytes.
+constexpr int kPushThreads = 512;
+constexpr int kRows = 8;
+
+template <bool VEC>
+__global__ void __launch_bounds__(kPushThreads) peer_push_kernel(const __grid_constant__ PushArgs A) {
+  typedef typename std::conditional<VEC, int4, int8_t>::type U;
+  constexpr int unit = VEC ? 16 : 1;
+  const int per_row = (int)(A.cols / unit);
+  const int c_units = (int)((A.split ? A.cols / A.n : A.cols) / unit);
+  for (int64_t r0 = blockIdx.x; r0 < A.rows; r0 += (int64_t)gridDim.x * kRows) {
+    for (int j = threadIdx.x; j < per_row; j += kPushThreads) {
+      U v[kRows];
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        const int64_t r = r0 + (int64_t)i * gridDim.x;
+        if (r < A.rows) v[i] = reinterpret_cast<const U*>(A.src + r * A.ld_src)[j];
+      }
+      const int p0 = A.split ? j / c_units : 0;
+      const int jd = j - p0 * c_units;
+#pragma unroll
+      for (int i = 0; i < kRows; ++i) {
+        const int64_t r = r0 + (int64_t)i * gridDim.x;
+        if (r >= A.rows) break;
+        const int64_t drow = (A.dst_row0 + r) * A.ld_dst;
+        if (A.split) {
+          reinterpret_cast<U*>(A.dst[p0] + drow)[jd] = v[i];
+        } else {
+#pragma unroll 1
+          for (int p = 0; p < A.n; ++p) reinterpret_cast<U*>(A.dst[p] + drow)[j] = v[i];
+        }
+      }
+    }
+  }
+}
+
+struct FlagArgs {
+  int64_t* peer_flags[ECO_MAX_PEERS];
+};
+
+ECO_DEV void st_release_sys(int64_t* p, int64_t v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+ECO_DEV int64_t ld_acquire_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+ECO_DEV unsigned long long peer_clock() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Thread p publishes `epoch` in slot (slot, rank) of rank p's flag array, after
+// everything this stream did before (the previous kernels' stores included).
+__global__ void peer_signal_kernel(const __grid_constant__ FlagArgs F, int n, int rank, int slot, int64_t epoch) {
+  const int p = threadIdx.x;
+  if (p >= n) return;
+  asm volatile("fence.sc.sys;" ::: "memory");
+  st_release_sys(F.peer_flags[p] + (int64_t)slot * ECO_MAX_PEERS + rank, epoch);
+}
+
+// Thread p waits until rank p's entry of `slot` in this rank's flags reaches `epoch`.
+__global__ void peer_wait_kernel(const int64_t* flags, int n, int slot, int64_t epoch, unsigned long long limit_ns) {
+  const int p = threadIdx.x;
+  if (p >= n) return;
+  const int64_t* f = flags + (int64_t)slot * ECO_MAX_PEERS + p;
+  if (ld_acquire_sys(f) >= epoch) return;
+  const unsigned long long t0 = peer_clock();
+  while (ld_acquire_sys(f) < epoch) {
+    if (peer_clock() - t0 > limit_ns) {
+      atomicOr(&g_peer_errors, ECO_FLAG_WAIT_TIMEOUT);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+}  // namespace
+
+// Sticky flags of the peer waits, cleared by the read (used by eco_read_device_errors).
+int eco_peer_errors_take(unsigned* out) {
+  unsigned zero = 0;
+  if (cudaMemcpyFromSymbol(out, g_peer_errors, sizeof(*out)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_peer_errors, &zero, sizeof(zero)) != cudaSuccess)
+    return eco_launch_check("eco_read_device_errors (peer)");
+  return ECO_OK;
+}
+
+extern "C" int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst,
+                                int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas,
+                                eco_stream_t stream) {
+  ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && ld_src >= cols && dst_row0 >= 0, ECO_ERR_ARG,
+              "eco_peer_push_s8: bad arguments");
+  ECO_REQUIRE(n_dst >= 1 && n_dst <= ECO_MAX_PEERS, ECO_ERR_ARG, "eco_peer_push_s8: 1..%d destinations",
+              ECO_MAX_PEERS);
+  ECO_REQUIRE(!split || cols % n_dst == 0, ECO_ERR_ARG, "eco_peer_push_s8: split needs cols divisible by n_dst");
+  ECO_REQUIRE(ld_dst >= (split ? cols / n_dst : cols), ECO_ERR_ARG, "eco_peer_push_s8: ld_dst too small");
+  if (rows == 0 || cols == 0) return ECO_OK;
+  PushArgs A;
+  A.src = src;
+  A.ld_src = ld_src;
+  A.rows = rows;
+  A.cols = cols;
+  A.ld_dst = ld_dst;
+  A.dst_row0 = dst_row0;
+  A.n = n_dst;
+  A.split = split;
+  bool vec = cols % 16 == 0 && ld_src % 16 == 0 && ld_dst % 16 == 0 && eco_aligned16(src) &&
+             (!split || (cols / n_dst) % 16 == 0);
+  for (int p = 0; p < ECO_MAX_PEERS; ++p) {
+    A.dst[p] = p < n_dst ? dst[p] : nullptr;
+    if (p < n_dst) {
+      ECO_REQUIRE(dst[p], ECO_ERR_ARG, "eco_peer_push_s8: null destination %d", p);
+      vec = vec && eco_aligned16(dst[p]);
+    }
+  }
+  ECO_REQUIRE(cols < (1ll << 31), ECO_ERR_ARG, "eco_peer_push_s8: too many columns");
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(rows, ctas > 0 ? ctas : eco_num_sms()));
+  if (vec)
+    peer_push_kernel<true><<<(unsigned)grid, kPushThreads, 0, eco_stream(stream)>>>(A);
+  else
+    peer_push_kernel<false><<<(unsigned)grid, kPushThreads, 0, eco_stream(stream)>>>(A);
+  return eco_launch_check("eco_peer_push_s8");
+}
+
+extern "C" int eco_peer_signal(int64_t* const* peer_flags, int n, int rank, int slot, int64_t epoch,
+                               eco_stream_t stream) {
+  ECO_REQUIRE(peer_flags && n >= 1 && n <= ECO_MAX_PEERS && rank >= 0 && rank < n && slot >= 0 && epoch > 0,
+              ECO_ERR_ARG, "eco_peer_signal: bad arguments");
+  FlagArgs F;
+  for (int p = 0; p < ECO_MAX_PEERS; ++p) {
+    F.peer_flags[p] = p < n ? peer_flags[p] : nullptr;
+    if (p < n) ECO_REQUIRE(peer_flags[p], ECO_ERR_ARG, "eco_peer_signal: null flag array %d", p);
+  }
+  peer_signal_kernel<<<1, 32, 0, eco_stream(stream)>>>(F, n, rank, slot, epoch);
+  return eco_launch_check("eco_peer_signal");
+}
+
+extern "C" int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, int64_t timeout_us,
+                             eco_stream_t stream) {
+  ECO_REQUIRE(flags && n >= 1 && n <= ECO_MAX_PEERS && slot >= 0 && epoch > 0 && timeout_us >= 0, ECO_ERR_ARG,
+              "eco_peer_wait: bad arguments");
+  const unsigned long long limit = timeout_us > 0 ? std::min<unsigned long long>((unsigned long long)timeout_us * 1000ull,
+                                                                                kPeerWaitNs)
+                                                  : kPeerWaitNs;
+  peer_wait_kernel<<<1, 32, 0, eco_stream(stream)>>>(flags, n, slot, epoch, limit);
+  return eco_launch_check("eco_peer_wait");
+}

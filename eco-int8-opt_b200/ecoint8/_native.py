@@ -59,6 +59,9 @@ _SIGS = {
                                        c_p, c_p]),
     "eco_set_gemm_sm_limit": (c_i32, [c_i32]),
     "eco_split_cols_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_i64, c_p, c_p]),
+    "eco_peer_push_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, c_i64, c_i64, c_i32, c_i32, c_p]),
+    "eco_peer_signal": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i64, c_p]),
+    "eco_peer_wait": (c_i32, [c_p, c_i32, c_i32, c_i64, c_i64, c_p]),
     "eco_gemm_s8_requant": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_p, c_i32,
                                     c_i32, SRSpec, c_p, c_i64, c_p]),
     "eco_requant_s32_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_p, c_i64, c_i32, c_i32, SRSpec, c_p, c_i64,

@@ -1,0 +1,161 @@
+"""The "peer" exchange of data parallelism: NVLink stores into buffers that every
+rank allocates and maps (torch symmetric memory), ordered by flag barriers.
+
+Per row-sharded layer every rank holds
+
+* ``x``: the layer's int8 input over the global batch ``[world * b, in]``; each
+  rank's forward pushes its ``b`` rows into every rank's copy;
+* ``dy``: its dY columns over the global batch ``[world * b, out / world]``;
+  each rank's backward pushes column block ``p`` of its dY rows to rank ``p``;
+* ``w``: the weights themselves (the layer's ``w_i8`` buffer moves here); after
+  the optimizer step each rank pushes its updated rows to the other ranks.
+
+Pushes run on a communication stream with a few CTAs; each is followed by a
+signal that writes an epoch into a flag slot on every rank, and consumers wait
+for the slot on their own stream (``eco_peer_wait``, bounded).  The dW GEMM of
+a layer runs on a third stream once the layer's inputs and dY columns of every
+rank have arrived, so the dX chain never waits for the exchange.
+
+Buffer reuse is ordered by the exchange itself: a rank only overwrites a peer's
+``x``/``dy`` in the next step's forward/backward, which every rank reaches only
+after the all-reduce of the dW maxima, which needs every rank's dW GEMM to have
+read those buffers; the weight rows are pushed after that same all-reduce and
+read by the next forward after its wait.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import weakref
+
+import torch
+import torch.distributed as dist
+
+from . import _native as nat
+
+MAX_PEERS = 8  # ECO_MAX_PEERS of the C ABI
+MAX_SLOTS = 3 * 256  # three flag slots per row-sharded layer
+
+
+def _arr(ptrs):
+    return (ctypes.c_void_p * len(ptrs))(*ptrs)
+
+
+class Shared:
+    """A tensor allocated on every rank of ``group`` with the device pointers of all copies.
+    Collective: every rank creates the same sequence of them."""
+
+    def __init__(self, shape, dtype, device, group):
+        from torch.distributed import _symmetric_memory as symm
+
+        self.t = symm.empty(*shape, dtype=dtype, device=device)
+        self.handle = symm.rendezvous(self.t, group)
+        h = self.handle
+        off = self.t.data_ptr() - h.buffer_ptrs[h.rank]
+        self.ptrs = [int(b) + off for b in h.buffer_ptrs]
+
+
+class LayerBufs:
+    def __init__(self, ex: "Exchange", layer, b: int):
+        idx = len(ex.layers)
+        if 3 * idx + 3 > MAX_SLOTS:
+            raise RuntimeError("ecoint8.parallel: too many row-sharded layers for the peer exchange")
+        self.slot_x, self.slot_dy, self.slot_w = 3 * idx, 3 * idx + 1, 3 * idx + 2
+        n, dev, g = ex.n, ex.dev, ex.group
+        out, in_f = layer.w_i8.shape
+        self.b, self.out, self.in_f = b, out, in_f
+        self.x = Shared((n * b, in_f), torch.int8, dev, g)
+        self.dy = Shared((n * b, out // n), torch.int8, dev, g)
+        self.w = Shared((out, in_f), torch.int8, dev, g)
+        self.w.t.copy_(layer.w_i8)
+        layer._buffers["w_i8"] = self.w.t  # the weights live in the shared buffer from now on
+        self.layer = weakref.ref(layer)
+        self.x_ptrs = _arr(self.x.ptrs)
+        self.dy_ptrs = _arr(self.dy.ptrs)
+        self.w_peers = _arr([p for r, p in enumerate(self.w.ptrs) if r != ex.rank])
+
+
+class Exchange:
+    """Flags, epochs, streams and per-layer buffers of one process."""
+
+    def __init__(self, group, device, push_ctas: int = 16):
+        self.group = group
+        self.ctas = push_ctas  # CTAs per push kernel: the rest of the GPU keeps running the GEMMs
+        self.n = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.n > MAX_PEERS:
+            raise RuntimeError(f"the peer exchange supports up to {MAX_PEERS} ranks")
+        self.dev = device
+        from torch.distributed import _symmetric_memory as symm
+
+        if hasattr(symm, "enable_symm_mem_for_group") and not symm.is_symm_mem_enabled_for_group(group.group_name):
+            symm.enable_symm_mem_for_group(group.group_name)
+        self.flags = Shared((MAX_SLOTS, MAX_PEERS), torch.int64, device, group)
+        self.flags.t.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+        self.flag_ptrs = _arr(self.flags.ptrs)
+        self.epoch = [0] * MAX_SLOTS
+        self.comm = torch.cuda.Stream(device)
+        self.dw = torch.cuda.Stream(device)
+        self.layers: dict[int, LayerBufs] = {}
+
+    # -- flags ------------------------------------------------------------------
+    def signal(self, slot: int, stream) -> None:
+        self.epoch[slot] += 1
+        nat.call("eco_peer_signal", self.flag_ptrs, self.n, self.rank, slot, self.epoch[slot], stream.cuda_stream)
+
+    def wait(self, slot: int, stream) -> None:
+        if self.epoch[slot] > 0:
+            nat.call("eco_peer_wait", self.flags.t.data_ptr(), self.n, slot, self.epoch[slot], 0, stream.cuda_stream)
+
+    def _after_current(self, stream) -> None:
+        stream.wait_stream(torch.cuda.current_stream(self.dev))
+
+    # -- layers -----------------------------------------------------------------
+    def layer(self, layer, b: int) -> LayerBufs:
+        bufs = self.layers.get(id(layer))
+        if bufs is None:
+            bufs = self.layers[id(layer)] = LayerBufs(self, layer, b)
+        elif bufs.b != b:
+            raise RuntimeError(f"the peer exchange needs a fixed per-rank batch ({bufs.b}), got {b}")
+        return bufs
+
+    def push_input(self, bufs: LayerBufs, x: torch.Tensor) -> None:
+        """This rank's input rows into every rank's ``x`` (rows rank * b ...)."""
+        self._after_current(self.comm)
+        nat.call("eco_peer_push_s8", x.data_ptr(), x.stride(0) if x.shape[0] > 1 else x.shape[1], x.shape[0],
+                 x.shape[1], bufs.x_ptrs, self.n, bufs.in_f, self.rank * bufs.b, 0, self.ctas,
+                 self.comm.cuda_stream)
+        self.signal(bufs.slot_x, self.comm)
+        x.record_stream(self.comm)
+
+    def push_grad_columns(self, bufs: LayerBufs, g: torch.Tensor) -> None:
+        """Column block p of this rank's dY rows into rank p's ``dy`` (rows rank * b ...)."""
+        self._after_current(self.comm)
+        nat.call("eco_peer_push_s8", g.data_ptr(), g.stride(0) if g.shape[0] > 1 else g.shape[1], g.shape[0],
+                 g.shape[1], bufs.dy_ptrs, self.n, bufs.out // self.n, self.rank * bufs.b, 1, self.ctas,
+                 self.comm.cuda_stream)
+        self.signal(bufs.slot_dy, self.comm)
+        g.record_stream(self.comm)
+
+    def push_weight_rows(self, bufs: LayerBufs, lo: int, hi: int) -> None:
+        """This rank's updated weight rows into the other ranks' ``w``."""
+        self._after_current(self.comm)
+        w = bufs.w.t
+        nat.call("eco_peer_push_s8", w.data_ptr() + lo * bufs.in_f, bufs.in_f, hi - lo, bufs.in_f, bufs.w_peers,
+                 self.n - 1, bufs.in_f, lo, 0, self.ctas, self.comm.cuda_stream)
+        self.signal(bufs.slot_w, self.comm)
+
+    def wait_weights(self, bufs: LayerBufs) -> None:
+        self.wait(bufs.slot_w, torch.cuda.current_stream(self.dev))
+
+    def release(self) -> None:
+        """Give every layer a private copy of its weights again."""
+        torch.cuda.synchronize(self.dev)
+        for bufs in self.layers.values():
+            layer = bufs.layer()
+            if layer is not None and layer._buffers.get("w_i8") is bufs.w.t:
+                layer._buffers["w_i8"] = bufs.w.t.clone()
+        torch.cuda.synchronize(self.dev)
+        self.layers.clear()

@@ -31,6 +31,10 @@ Two ways of forming the summed dW rows (``init(dw_exchange=...)``):
   computes its own dW rows over the whole global batch in one GEMM (the same
   exact int32 sums; about half the bytes of the reduce-scatter, and no full-size
   int32 dW in HBM).  Needs the same batch size on every rank.
+* ``"peer"``: the same data as ``"gather"``, moved by the library's own kernels
+  as NVLink stores into buffers mapped on every rank (``_peer``), with flag
+  barriers; the weight rows after the step travel the same way.  NCCL only
+  carries the small maxima and sums.
 
 A layer is row-sharded when its output count divides evenly by the world size
 (at least 8 rows per rank); other layers all-reduce their dW and step every row
@@ -53,28 +57,32 @@ _GROUP = None  # large transfers (dW, weights)
 _SMALL = None  # scalar / small-vector collectives
 _ACT = None  # activation all-gathers and dY all-to-all ("gather" exchange)
 _EXCHANGE = "reduce"
+_PEER = None  # _peer.Exchange of the "peer" exchange, created on first use
+_PUSH_CTAS = [16]
 _PENDING: list = []  # layers whose dW reduction is in flight
 COMM_SMS = 16  # SMs the GEMMs leave free for NCCL while data parallelism is active
 
 
-def init(group=None, comm_sms: int = COMM_SMS, dw_exchange: str = "reduce") -> None:
+def init(group=None, comm_sms: int = COMM_SMS, dw_exchange: str = "reduce", push_ctas: int = 16) -> None:
     """Enable the exchanges on ``group`` (default: the world).  Collective: call on every rank.
 
-    ``comm_sms``: SMs the persistent GEMMs leave to NCCL, so the dW
+    ``comm_sms``: SMs the persistent GEMMs leave to the exchange, so the dW
     reduce-scatter and the weight all-gather overlap the GEMMs instead of
-    waiting for them to finish.  ``dw_exchange``: ``"reduce"`` or ``"gather"``
-    (module docstring).
+    waiting for them to finish.  ``dw_exchange``: ``"reduce"``, ``"gather"`` or
+    ``"peer"`` (module docstring).  ``push_ctas``: CTAs of each push kernel of
+    the peer exchange.
     """
     global _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE
     if not dist.is_initialized():
         raise RuntimeError("ecoint8.parallel.init needs torch.distributed to be initialized")
-    if dw_exchange not in ("reduce", "gather"):
-        raise ValueError(f"dw_exchange must be 'reduce' or 'gather', got {dw_exchange!r}")
+    if dw_exchange not in ("reduce", "gather", "peer"):
+        raise ValueError(f"dw_exchange must be 'reduce', 'gather' or 'peer', got {dw_exchange!r}")
     _GROUP = group
     ranks = list(range(dist.get_world_size())) if group is None else dist.get_process_group_ranks(group)
     _SMALL = dist.new_group(ranks=ranks)
     _ACT = dist.new_group(ranks=ranks) if dw_exchange == "gather" else None
     _EXCHANGE = dw_exchange
+    _PUSH_CTAS[0] = int(push_ctas)
     _ACTIVE = True
     if torch.cuda.is_available() and comm_sms > 0 and len(ranks) > 1:
         from . import _native
@@ -84,9 +92,11 @@ def init(group=None, comm_sms: int = COMM_SMS, dw_exchange: str = "reduce") -> N
 
 
 def shutdown() -> None:
-    global _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE
+    global _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE, _PEER
     finalize_pending()
-    _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE = False, None, None, None, "reduce"
+    if _PEER is not None:
+        _PEER.release()
+    _ACTIVE, _GROUP, _SMALL, _ACT, _EXCHANGE, _PEER = False, None, None, None, "reduce", None
     if torch.cuda.is_available():
         from . import _native
 
@@ -202,6 +212,55 @@ def exchange_grad_columns(g_i8: torch.Tensor):
     return exchange_blocks(column_blocks(g_i8))
 
 
+# -- "peer" exchange --------------------------------------------------------------
+def peer_bufs(layer, b: int | None = None):
+    """The peer-exchange buffers of a row-sharded layer (created on its first forward,
+    ``b`` = this rank's batch rows), or None when the layer does not use them."""
+    global _PEER
+    if not (active() and _EXCHANGE == "peer" and shard_rows(layer.out_features) is not None):
+        return None
+    if _PEER is None:
+        if b is None:
+            return None
+        from . import _peer
+
+        _PEER = _peer.Exchange(_GROUP if _GROUP is not None else dist.group.WORLD, layer.w_i8.device,
+                               _PUSH_CTAS[0])
+    if b is None:
+        return _PEER.layers.get(id(layer))
+    return _PEER.layer(layer, b)
+
+
+def peer_forward(layer, x_i8: torch.Tensor) -> None:
+    """Before a row-sharded layer's forward GEMM: wait for the other ranks' weight
+    rows of the last step, then push this rank's input rows to every rank."""
+    bufs = peer_bufs(layer, x_i8.shape[0])
+    _PEER.wait_weights(bufs)
+    _PEER.push_input(bufs, _ops._rowmajor(x_i8))
+
+
+def start_dw_rows_peer(layer, g_i8: torch.Tensor, s_g: float) -> None:
+    """Push this rank's dY column blocks, then (on the exchange's dW stream, once
+    every rank's inputs and dY columns have arrived) this rank's dW rows in one
+    GEMM over the global batch, their max|.| and the bias column sums."""
+    bufs = peer_bufs(layer)
+    ex = _PEER
+    ex.push_grad_columns(bufs, _ops._rowmajor(g_i8))
+    lo, hi = shard_rows(bufs.out)
+    dws = ex.dw
+    with torch.cuda.stream(dws):
+        ex.wait(bufs.slot_x, dws)
+        ex.wait(bufs.slot_dy, dws)
+        amax = torch.empty(1, dtype=torch.int32, device=bufs.x.t.device)
+        red = _ops.gemm_s32(bufs.dy.t, 1, bufs.x.t, 1, hi - lo, bufs.in_f, bufs.x.t.shape[0], amax=amax)
+        gb_rows = _ops.colsum(bufs.dy.t)
+        done = torch.cuda.Event()
+        done.record(dws)
+    layer._dw_pending = {"red": red, "full": None, "shape": (bufs.out, bufs.in_f), "work": None, "gb": None,
+                         "gb_rows": gb_rows, "event": done, "rows": (lo, hi), "s_g": float(s_g), "amax": amax}
+    _PENDING.append(layer)
+
+
 def start_dw_rows(layer, dy_cols: torch.Tensor, a2a, s_g: float) -> None:
     """This rank's rows of the summed dW in one GEMM over the global batch ("gather" exchange)."""
     full, xwork = layer._input_gather
@@ -242,6 +301,16 @@ def finalize_pending() -> None:
         return
     layers = list(_PENDING)
     _PENDING.clear()
+    cur = torch.cuda.current_stream() if torch.cuda.is_available() else None
+    for l in layers:  # dW rows formed on the peer exchange's stream
+        p = l._dw_pending
+        if p.get("event") is not None:
+            cur.wait_event(p["event"])
+            for t in (p["red"], p["amax"], p["gb_rows"]):
+                t.record_stream(cur)
+            lo, hi = p["rows"]
+            p["gb"] = torch.zeros(p["shape"][0], dtype=torch.int64, device=p["red"].device)
+            p["gb"][lo:hi] = p["gb_rows"]  # the other rows arrive through the flat SUM below
     # the bias column sums of every pending layer in one all-reduce
     gbs = [l._dw_pending["gb"] for l in layers]
     flat = torch.cat(gbs)
@@ -285,6 +354,10 @@ def combine_step_state(state: torch.Tensor) -> None:
 def gather_rows(layer, rows) -> None:
     """All-gather this rank's updated weight rows (asynchronous; the biases are
     stepped in full on every rank)."""
+    bufs = peer_bufs(layer)
+    if bufs is not None:
+        _PEER.push_weight_rows(bufs, rows[0], rows[1])
+        return
     layer._gather_works = [dist.all_gather_into_tensor(layer.w_i8, layer.w_i8[rows[0]:rows[1]], group=_GROUP,
                                                        async_op=True)]
 
@@ -295,6 +368,9 @@ def gather_flat(flat: torch.Tensor):
 
 
 def wait_gathers(layer) -> None:
+    bufs = peer_bufs(layer) if _PEER is not None else None
+    if bufs is not None:
+        _PEER.wait_weights(bufs)
     works = layer.__dict__.get("_gather_works")
     if works:
         for w in works:

@@ -258,9 +258,12 @@ class I8Linear(nn.Module):
         _check_int(x_i8, "layer input")
         _native.require_cuda(x_i8, self.w_i8)
         assert isinstance(self.sx, float) and isinstance(self.sy, float)
-        parallel.wait_gathers(self)
-        if parallel.gathers_input(self):
-            parallel.gather_input(self, x_i8)  # the global-batch input of this layer's dW ("gather" exchange)
+        if parallel.peer_bufs(self, x_i8.shape[0]) is not None:
+            parallel.peer_forward(self, x_i8)  # weight rows in, input rows out ("peer" exchange)
+        else:
+            parallel.wait_gathers(self)
+            if parallel.gathers_input(self):
+                parallel.gather_input(self, x_i8)  # the global-batch input of this layer's dW ("gather" exchange)
         mults, com = self._fwd_mults(x_i8.device)
         N, K = x_i8.shape
         out = self.out_features
@@ -334,14 +337,19 @@ class I8Linear(nn.Module):
         draws and results as the single-device backward on the concatenated batch."""
         N, out = g_i8.shape
         in_f = x_i8.shape[1]
+        peer = parallel.peer_bufs(self) is not None
         gathered = self.__dict__.get("_input_gather") is not None
-        if gathered:
+        if peer:  # dY columns out, then the dW GEMM on the exchange's stream once all have arrived
+            parallel.start_dw_rows_peer(self, g_i8, s_g)
+        elif gathered:
             dy_cols, a2a = parallel.exchange_grad_columns(g_i8)
         else:
             dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N)
             gb_sum = _ops.colsum(g_i8)
         key_w = _sr.reserve_key()  # the dW site's key, in the reference's draw order
-        if not gathered:
+        if peer:
+            self._dw_pending["key"] = key_w
+        elif not gathered:
             parallel.start_dw_reduction(self, dw_acc, gb_sum, s_g)
             self._dw_pending["key"] = key_w
         self._gb_s = float(s_g)

@@ -140,8 +140,8 @@ ECO_API int eco_amax(const void* x, int x_bits, int64_t n, int64_t* out, eco_str
 ECO_API int eco_sumsq_s8(const int8_t* x, int64_t n, int64_t* out, eco_stream_t stream);
 
 /* Reads and clears the sticky device error flags (bit 4: a bounded device wait
- * gave up).  Synchronises the device.  No reference counterpart: the reference
- * has no device-side waits. */
+ * gave up, in a GEMM pipeline or a peer-exchange wait).  Synchronises the
+ * device.  No reference counterpart: the reference has no device-side waits. */
 ECO_API int eco_read_device_errors(uint32_t* flags);
 
 /* 2-D strided int8 copy (relayout to a 16-byte aligned leading dimension). */
@@ -155,6 +155,35 @@ ECO_API int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_
  * data parallelism). */
 ECO_API int eco_split_cols_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int64_t parts,
                       int8_t* dst, eco_stream_t stream);
+
+/* ------------------------------------------ data-parallel peer exchange -----
+ * No reference counterpart (the reference has no data parallelism).  The buffers
+ * are allocated on every rank and mapped into each process (each rank holds
+ * device pointers to all ranks' copies); these calls move the exchange of the
+ * data-parallel backward over NVLink with plain stores issued by a few CTAs,
+ * and publish completion through flag words.  All waits are bounded (5 s): on
+ * expiry the wait records bit 4 in the sticky device error flags
+ * (eco_read_device_errors) and returns. */
+#define ECO_MAX_PEERS 8
+
+/* Pushes a [rows, cols] int8 matrix into n_dst destination buffers (device
+ * pointers, host array) at rows dst_row0.. with leading dimension ld_dst.
+ * split = 0: every destination receives the whole matrix (an all-gather of row
+ * blocks); split = 1: destination p receives columns [p*c, (p+1)*c), c = cols /
+ * n_dst (an all-to-all of column blocks).  ctas bounds the grid (0: one per SM). */
+ECO_API int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst,
+                     int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas, eco_stream_t stream);
+
+/* Flag arrays are int64 [slots, ECO_MAX_PEERS], zero before first use.  signal:
+ * after all prior work on the stream, writes epoch into entry (slot, rank) of
+ * every rank's array (peer_flags: host array of the n ranks' flag pointers).
+ * wait: the stream continues once entries (slot, 0..n-1) of this rank's array
+ * all reach epoch (epochs only grow), or after timeout_us (0: the 5 s limit;
+ * larger values are capped at it). */
+ECO_API int eco_peer_signal(int64_t* const* peer_flags, int n, int rank, int slot, int64_t epoch,
+                    eco_stream_t stream);
+ECO_API int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, int64_t timeout_us,
+                  eco_stream_t stream);
 
 /* -------------------------------------------------------- I8ECO step -----
  * One fused, single-pass integer ECO-SGDM step over a list of layers

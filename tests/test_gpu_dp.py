@@ -1,5 +1,6 @@
 """Data parallelism on 2 GPUs reproduces the single-GPU run bit for bit (NCCL),
-with either dW exchange (int32 reduce-scatter, or gathered inputs + dY all-to-all).
+with every dW exchange (int32 reduce-scatter; gathered inputs + dY all-to-all
+through NCCL; the same through the library's NVLink peer stores).
 
 Two ranks split a batch of 96 rows; rank 0 also trains an identical net on the
 whole batch on its own.  Both use the same Philox key sequence, so after
@@ -91,7 +92,7 @@ def _worker(rank, port, q):
         X8, sx = quantize_tensor_dynamic(X)  # entry scale of the global batch, identical on both ranks
         lo, hi = rank * B // 2, (rank + 1) * B // 2
         runs = {}
-        for exchange in ("reduce", "gather"):
+        for exchange in ("reduce", "gather", "peer"):
             parallel.init(dw_exchange=exchange)
             net = _net(dev)
             opt = _train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), 2, lo, 123, 4)
@@ -135,4 +136,4 @@ def test_two_gpu_data_parallel_equals_single_gpu():
     for p in ps:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert ok == {"reduce": True, "gather": True}
+    assert ok == {"reduce": True, "gather": True, "peer": True}

@@ -172,6 +172,41 @@ def test_split_cols_matches_block_transpose():
         assert torch.equal(dst, want), (rows, cols, parts)
 
 
+def test_peer_push_signal_and_bounded_wait_on_one_gpu():
+    """The peer-exchange kernels with this GPU's own buffers as the only 'peer': both
+    push modes land where the layout says, a signalled slot releases the wait, and
+    a slot nobody signals times out into the sticky error flags (no hang)."""
+    import ctypes
+
+    from ecoint8 import _native
+
+    s = _native.stream()
+    gen = torch.Generator().manual_seed(4)
+    for rows, cols in [(48, 40), (64, 256)]:
+        src = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, generator=gen).cuda()
+        dst = torch.zeros((3 * rows, cols), dtype=torch.int8, device="cuda")
+        arr = (ctypes.c_void_p * 1)(dst.data_ptr())
+        _native.call("eco_peer_push_s8", src.data_ptr(), cols, rows, cols, arr, 1, cols, rows, 0, 4, s)
+        assert torch.equal(dst[rows:2 * rows], src) and not dst[:rows].any() and not dst[2 * rows:].any()
+        dsts = [torch.zeros((2 * rows, cols // 2), dtype=torch.int8, device="cuda") for _ in range(2)]
+        arr = (ctypes.c_void_p * 2)(*[d.data_ptr() for d in dsts])
+        _native.call("eco_peer_push_s8", src.data_ptr(), cols, rows, cols, arr, 2, cols // 2, rows, 1, 4, s)
+        for p, d in enumerate(dsts):
+            assert torch.equal(d[rows:], src[:, p * cols // 2:(p + 1) * cols // 2]) and not d[:rows].any()
+    flags = torch.zeros((4, 8), dtype=torch.int64, device="cuda")
+    fl = (ctypes.c_void_p * 1)(flags.data_ptr())
+    torch.cuda.synchronize()
+    assert _native.read_device_errors() == 0
+    _native.call("eco_peer_signal", fl, 1, 0, 2, 7, s)
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 2, 7, 100000, s)
+    torch.cuda.synchronize()
+    assert int(flags[2, 0]) == 7 and _native.read_device_errors() == 0
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 3, 1, 100000, s)  # nothing signals slot 3
+    torch.cuda.synchronize()
+    assert _native.read_device_errors() == 4
+    assert _native.read_device_errors() == 0  # the read clears the flags
+
+
 def test_library_reports_no_device_timeouts():
     from ecoint8 import _native
 
