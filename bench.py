@@ -219,8 +219,9 @@ def gemm_measurements(device):
 
 
 def requant_measurement(device, rows=16384, cols=8192):
-    """The dX requant of one 8192-wide layer at batch 16384: int32 -> int8, Philox SR,
-    scalar multiplier, ReLU mask and square sum (4 + 1 + 1 B per element)."""
+    """The two backward requants of one 8192-wide layer at batch 16384, as training runs
+    them: dX (int32 -> int8, Philox SR, scalar multiplier, ReLU mask; 4 + 1 + 1 B per
+    element) and dW (8192 x 8192, square sum for the gradient clip; 4 + 1 B)."""
     from ecoint8 import _native, _ops, _sr
 
     gen = torch.Generator(device=device).manual_seed(3)
@@ -228,9 +229,13 @@ def requant_measurement(device, rows=16384, cols=8192):
     mask = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, device=device, generator=gen)
     sq = torch.empty(1, dtype=torch.int64, device=device)
     site = _sr.Site(_native.sr_spec(_native.SR_PHILOX, seed=11, stream_id=0), None)
-    t = time_kernel(lambda: _ops.requant(src, 1 << 30, 38, site, mask=mask, sumsq=sq))
+    t = time_kernel(lambda: _ops.requant(src, 1 << 30, 38, site, mask=mask))
+    w = src[:cols]
+    t_w = time_kernel(lambda: _ops.requant(w, 1 << 30, 38, site, sumsq=sq))
     n = rows * cols
-    return {"shape": [rows, cols], "ms": t * 1e3, "gbs": 6.0 * n / t / 1e9, "bytes_per_element": 6}
+    return {"shape": [rows, cols], "ms": t * 1e3, "gbs": 6.0 * n / t / 1e9, "bytes_per_element": 6,
+            "dw": {"shape": [cols, cols], "ms": t_w * 1e3, "gbs": 5.0 * cols * cols / t_w / 1e9,
+                   "bytes_per_element": 5}}
 
 
 def eco_step_measurement(device, layers=64, dim=4096, steps=5):
@@ -425,16 +430,34 @@ def main():
         ms = ev0.elapsed_time(ev1)
         launches = counter.count // args.steps
         # e2e: the same steps through the public API with the int8 batch and labels coming
-        # from pinned host memory and the loss read back every step
+        # from pinned host memory and the loss read back every step; like a data loader,
+        # the next step's batch crosses PCIe on a copy stream while this step computes
         x_host = x_i8.cpu().pin_memory()
         y_host = y.cpu().pin_memory()
+        copy_stream = torch.cuda.Stream(device)
+        cur = torch.cuda.current_stream(device)
+
+        def fetch():
+            with torch.cuda.stream(copy_stream):
+                xb = x_host.to(device, non_blocking=True)
+                yb = y_host.to(device, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+            return xb, yb, ev
+
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
-            xb = x_host.to(device, non_blocking=True)
-            yb = y_host.to(device, non_blocking=True)
+        copy_stream.wait_event(e0)  # the first batch's copy is inside the timed region too
+        nxt = fetch()
+        for i in range(args.steps):
+            xb, yb, ev = nxt
+            cur.wait_event(ev)
+            xb.record_stream(cur)
+            yb.record_stream(cur)
+            if i + 1 < args.steps:
+                nxt = fetch()
             loss = train_step(net, opt, xb, yb, world)
             float(loss.item())
         e1.record()

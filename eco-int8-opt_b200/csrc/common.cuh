@@ -38,6 +38,46 @@ ECO_DEV i64 ams(i64 x, i64 mult, int shift, i64 nudge) {
 ECO_DEV i64 half_nudge(int shift) { return shift > 0 ? (1ll << (shift - 1)) : 0; }
 ECO_DEV i64 low_bits(u64 w, int n) { return n <= 0 ? 0 : (n >= 64 ? (i64)w : (i64)(w & ((1ull << n) - 1))); }
 
+// 32x32 -> 64 products as single instructions (exact; two's complement sums).
+ECO_DEV i64 mul_wide_s32(int a, int b) {
+  i64 d;
+  asm("mul.wide.s32 %0, %1, %2;" : "=l"(d) : "r"(a), "r"(b));
+  return d;
+}
+ECO_DEV i64 mad_wide_s32(int a, int b, i64 c) {
+  i64 d;
+  asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c));
+  return d;
+}
+ECO_DEV i64 mad_wide_u32(uint32_t a, uint32_t b, i64 c) {  // c + a * b modulo 2^64
+  i64 d;
+  asm("mad.wide.u32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(c));
+  return d;
+}
+ECO_DEV int hi32(i64 x) { return (int)(x >> 32); }
+ECO_DEV uint32_t lo32(i64 x) { return (uint32_t)x; }
+// (int)(x >> s) for 0 <= s < 32 when the result fits int32: one funnel shift.
+ECO_DEV int shr_fit(i64 x, int s) { return (int)__funnelshift_r(lo32(x), (uint32_t)hi32(x), s); }
+
+// Bytes of `w` that are > 0 as signed int8 -> 0xFF, others 0x00 (no carries cross bytes).
+ECO_DEV uint32_t bytes_positive(uint32_t w) {
+  const uint32_t t = (w & 0x7F7F7F7Fu) + 0x7F7F7F7Fu;  // bit 7: low seven bits nonzero
+  const uint32_t k = t & ~w & 0x80808080u;            // ... and sign bit clear
+  return (k >> 7) * 0xFFu;
+}
+// Byte k (0..3) of x, sign-extended: one byte permute whose upper selector nibbles
+// replicate the byte's sign bit.
+ECO_DEV int sbyte(uint32_t x, int k) {
+  const uint32_t sel = (uint32_t)k | ((uint32_t)(k | 8) << 4) | ((uint32_t)(k | 8) << 8) | ((uint32_t)(k | 8) << 12);
+  uint32_t d;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(d) : "r"(x), "r"(sel));
+  return (int)d;
+}
+// Low bytes of four ints packed into one word.
+ECO_DEV uint32_t pack4(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 // ---------------------------------------------------------------- Philox4x32-10
 // Salmon et al., "Parallel random numbers: as easy as 1, 2, 3" (SC'11).
 struct Philox4 {
@@ -58,6 +98,42 @@ ECO_DEV Philox4 philox10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uin
     k1 += 0xBB67AE85u;
   }
   return Philox4{c0, c1, c2, c3};
+}
+
+// The ten round keys of a Philox4x32-10 key (key + i * Weyl constants), computed
+// once on the host.  Kernels keep them in their parameter block, so every round
+// XORs a constant-bank operand instead of advancing two key registers.
+struct PhiloxKeys {
+  uint32_t k0[10], k1[10];
+};
+static inline __host__ __device__ PhiloxKeys philox_keys(u64 seed) {
+  PhiloxKeys K;
+  uint32_t a = (uint32_t)seed, b = (uint32_t)(seed >> 32);
+  for (int i = 0; i < 10; ++i) {
+    K.k0[i] = a;
+    K.k1[i] = b;
+    a += 0x9E3779B9u;
+    b += 0xBB67AE85u;
+  }
+  return K;
+}
+ECO_DEV Philox4 philox10k(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, const PhiloxKeys& K) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const u64 p0 = (u64)0xD2511F53u * c0;
+    const u64 p1 = (u64)0xCD9E8D57u * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ K.k0[i];
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ K.k1[i];
+    c1 = (uint32_t)p1;
+    c3 = (uint32_t)p0;
+    c0 = n0;
+    c2 = n2;
+  }
+  return Philox4{c0, c1, c2, c3};
+}
+// sr_quad with precomputed round keys (same bits).
+ECO_DEV Philox4 sr_quad_k(const PhiloxKeys& K, u64 stream, uint32_t row, uint32_t quad) {
+  return philox10k(quad, row, (uint32_t)stream, (uint32_t)(stream >> 32), K);
 }
 
 // The library's stochastic-rounding stream: 64 random bits for the column

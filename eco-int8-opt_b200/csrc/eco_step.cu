@@ -38,6 +38,7 @@ struct LayerDesc {
 
 struct StepParams {
   eco_i8eco_hyper_t H;
+  PhiloxKeys keys;  // round keys of H.seed
   int n_layers;
   i64 total_tiles;
   LayerDesc layers[kMaxLayers];
@@ -180,6 +181,85 @@ ECO_DEV void eco_elem_fast(const FastRow& c, int w, int m, int g, int nw, int& m
   m_new_out = m_new;
 }
 
+// (x >> s) as int32 (the result fits): the high word shifted when s >= 32 (HI),
+// else one funnel shift.
+template <bool HI>
+ECO_DEV int shr_sel(i64 x, int s) {
+  return HI ? (hi32(x) >> (s - 32)) : shr_fit(x, s);
+}
+
+// One row of the step on the 32-bit path (row_is_fast holds, momentum shift in
+// 32..51): single-instruction 32x32->64 products, one shift per requant, bytes
+// unpacked and packed with byte permutes, and the momentum rounding's tie-break
+// draw taken only on its 2^-20 ties.  Each lane takes every 32nd 16-byte chunk,
+// with the next chunk's loads in flight.  Returns the row's max |m_new|; adds the
+// row's sum |e| to rsum.
+template <bool HM, bool HG>
+ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 stream, uint32_t row, int8_t* wr,
+                       int8_t* mr, const int8_t* gr, int nch, int lane, u64& rsum) {
+  const int mmu = (int)c.mult_m, mgu = (int)c.mult_g, mmm = (int)c.mult_mm;
+  const i64 hm = c.half_m, hg = c.half_g;
+  const int cm = c.com_m, cg = c.com_g, lo = c.com_mm - 20, shm = c.com_mm - 32;
+  const uint32_t p2lo = 1u << lo;
+  const int bq = (int)c.b_q, nbq = (int)c.nb_q, lrq = (int)c.lr_q, aq = (int)c.a_q;
+  int rmx = 0, rmn = 0;
+  int j = lane;
+  int4 wn4 = make_int4(0, 0, 0, 0), mn4 = wn4, gn4 = wn4;
+  if (j < nch) {
+    wn4 = *reinterpret_cast<const int4*>(wr + 16 * j);
+    mn4 = *reinterpret_cast<const int4*>(mr + 16 * j);
+    gn4 = *reinterpret_cast<const int4*>(gr + 16 * j);
+  }
+  for (; j < nch; j += 32) {
+    const int4 wv = wn4, mv = mn4, gv = gn4;
+    if (j + 32 < nch) {  // the next chunk's loads fly while this one computes
+      wn4 = *reinterpret_cast<const int4*>(wr + 16 * (j + 32));
+      mn4 = *reinterpret_cast<const int4*>(mr + 16 * (j + 32));
+      gn4 = *reinterpret_cast<const int4*>(gr + 16 * (j + 32));
+    }
+    const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+    const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mv);
+    const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
+    uint32_t wo[4], mo[4];
+    int rsum32 = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const Philox4 rnd = sr_quad_k(keys, stream, row, (uint32_t)(4 * j + q));
+      int wq[4], mq[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t f = quad_word(rnd, k);
+        const int w = sbyte(ww[q], k), m = sbyte(mw[q], k), g = sbyte(gw[q], k);
+        const int mU = shr_sel<HM>(mad_wide_s32(m, mmu, hm), cm);
+        const int gU = shr_sel<HG>(mad_wide_s32(g, mgu, hg), cg);
+        const int m_t = shr_fit(mad_wide_s32(gU, nbq, mul_wide_s32(mU, bq)), 16);
+        const int thU = w * 4096 - shr_fit(mul_wide_s32(m_t, lrq), 16);
+        const int wn = max(min((thU + (int)(f & 0xFFFu)) >> 12, 127), -127);
+        const int eU = thU - wn * 4096;
+        const int m_new = m_t + shr_fit(mul_wide_s32(eU, aq), 16);
+        rmx = max(rmx, m_new);
+        rmn = min(rmn, m_new);
+        rsum32 += abs(eU);
+        const i64 p2 = mad_wide_u32(f >> 12, p2lo, mul_wide_s32(m_new, mmm));
+        int y;
+        if ((__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) & 0xFFFFFu) != 0xFFFFFu)
+          y = hi32(p2) >> shm;
+        else
+          y = (int)max((i64)-128, min((i64)128, step_m_round_tie(p2, c.com_mm, seed, stream, row,
+                                                                (uint32_t)(16 * j + 4 * q + k))));
+        wq[k] = wn;
+        mq[k] = max(min(y, 127), -127);
+      }
+      wo[q] = pack4(wq[0], wq[1], wq[2], wq[3]);
+      mo[q] = pack4(mq[0], mq[1], mq[2], mq[3]);
+    }
+    rsum += (u64)(unsigned)rsum32;
+    *reinterpret_cast<int4*>(wr + 16 * j) = make_int4(wo[0], wo[1], wo[2], wo[3]);
+    *reinterpret_cast<int4*>(mr + 16 * j) = make_int4(mo[0], mo[1], mo[2], mo[3]);
+  }
+  return max(rmx, -rmn);
+}
+
 ECO_DEV i64 replay(const void* p, int bits, i64 idx) {
   return bits == 32 ? (i64)static_cast<const int32_t*>(p)[idx] : static_cast<const i64*>(p)[idx];
 }
@@ -267,7 +347,20 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
       int8_t* wr = L.w + r * L.cols;
       int8_t* mr = L.m + r * L.cols;
       const int8_t* gr = L.g + r * L.cols;
-      if (c.fast) {
+      const bool fast32 = c.fast && c.com_mm >= 32 && c.com_mm <= 51;
+      if (fast32) {
+        const bool hm = c.com_m >= 32, hg = c.com_g >= 32;
+        int rmx;
+        if (!hm && !hg)
+          rmx = fast32_row<false, false>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+        else if (hm && !hg)
+          rmx = fast32_row<true, false>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+        else if (!hm && hg)
+          rmx = fast32_row<false, true>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+        else
+          rmx = fast32_row<true, true>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+        rmax = rmx;
+      } else if (c.fast) {
         FastRow fr;
         fr.mult_m = (int)c.mult_m; fr.mult_g = (int)c.mult_g; fr.mult_mm = (int)c.mult_mm;
         fr.half_m = (int)c.half_m; fr.half_g = (int)c.half_g;
@@ -285,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
           int rsum32 = 0;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const Philox4 rnd = sr_quad(H.seed, L.stream_w, row, (uint32_t)((c0 >> 2) + q));
+            const Philox4 rnd = sr_quad_k(P.keys, L.stream_w, row, (uint32_t)((c0 >> 2) + q));
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int e = 4 * q + k;
@@ -307,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
         // exact int64 path: any shape, any alignment, replay mode, wide intermediates
         for (i64 c0 = 4 * lane; c0 < L.cols; c0 += 128) {
           Philox4 rnd{0u, 0u, 0u, 0u};
-          if (PHILOX) rnd = sr_quad(H.seed, L.stream_w, row, (uint32_t)(c0 >> 2));
+          if (PHILOX) rnd = sr_quad_k(P.keys, L.stream_w, row, (uint32_t)(c0 >> 2));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const i64 col = c0 + k;
@@ -399,6 +492,7 @@ extern "C" int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, con
   for (int base = 0; base < n_layers; base += kMaxLayers) {
     StepParams P;
     P.H = *hyper;
+    P.keys = philox_keys(hyper->seed);
     P.n_layers = std::min(kMaxLayers, n_layers - base);
     i64 tiles = 0;
     for (int i = 0; i < P.n_layers; ++i) {

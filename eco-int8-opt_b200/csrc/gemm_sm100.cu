@@ -65,6 +65,7 @@ struct GemmParams {
   eco_sr_t sr;
   int8_t* Y;
   i64 ldy;
+  PhiloxKeys keys;  // round keys of sr.seed
 };
 
 // Tile t of the grouped raster: kGroupM M-tiles share each N column block in turn.
@@ -193,7 +194,7 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     Philox4 rnd{0u, 0u, 0u, 0u};
-    if (philox) rnd = sr_quad(p.sr.seed, p.sr.stream, row, (uint32_t)((nb >> 2) + q));
+    if (philox) rnd = sr_quad_k(p.keys, p.sr.stream, row, (uint32_t)((nb >> 2) + q));
     packed[q] = 0u;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -507,6 +508,7 @@ extern "C" int eco_gemm_s8_requant(const int8_t* A, int64_t lda, int a_layout, c
   p.shift = shift;
   p.relu = relu;
   p.sr = sr;
+  p.keys = philox_keys(sr.seed);
   p.Y = Y;
   p.ldy = ldy;
   return gemm_common(A, lda, a_layout, B, ldb, b_layout, M, N, K, p, 1, eco_stream(stream), "eco_gemm_s8_requant");

@@ -72,6 +72,7 @@ struct RequantArgs {
   i64 ld_dst;
   i64* sumsq;
   int mult32;  // mult_scalar fits int32: 32x32->64 products
+  PhiloxKeys keys;  // round keys of sr.seed (Philox mode)
 };
 
 // MODE: 0 round half up, 1 Philox, 2 replay.  One thread handles 16 consecutive
@@ -153,72 +154,84 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
   const int cpr = (int)(a.cols >> 4);
   const int sh = a.shift;
   const int lo = sh - 32;  // BIG: bits of the tie-break draw
+  const uint32_t pow2lo = BIG ? 1u << lo : 0u;
+  const int lower = a.relu ? 0 : -127;
   const int32_t mult_s = (int32_t)a.mult_scalar;
   long long sq = 0;
-  for (i64 r = blockIdx.x; r < a.rows; r += gridDim.x) {
-    const uint32_t grow = (uint32_t)(a.sr.row_base + r);
-    const int32_t* srow = a.src + r * a.ld_src;
-    int8_t* drow = a.dst + r * a.ld_dst;
-    // software pipeline: the next chunk's loads are in flight while this one computes
-    int4 nx[4], nm = make_int4(0, 0, 0, 0);
-    int j = threadIdx.x;
-    if (j < cpr) {
+  // The block's work is the chunk sequence (row r, chunk j) with rows blockIdx.x +
+  // k * gridDim.x; thread t takes every blockDim.x-th chunk of it, and the next
+  // chunk's loads (possibly in the next row) are in flight while one computes.
+  i64 r = blockIdx.x;
+  int j = threadIdx.x;
+  while (j >= cpr && r < a.rows) {
+    j -= cpr;
+    r += gridDim.x;
+  }
+  int4 nx[4], nm = make_int4(0, 0, 0, 0);
+  if (r < a.rows) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(srow + j * 16)[q];
+    for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(a.src + r * a.ld_src + j * 16)[q];
+    if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + j * 16);
+  }
+  while (r < a.rows) {
+    const i64 cr = r;
+    const int c0 = j * 16;
+    int v[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[4 * q] = nx[q].x; v[4 * q + 1] = nx[q].y; v[4 * q + 2] = nx[q].z; v[4 * q + 3] = nx[q].w;
+    }
+    const int4 mk = nm;
+    j += blockDim.x;
+    while (j >= cpr && r < a.rows) {
+      j -= cpr;
+      r += gridDim.x;
+    }
+    if (r < a.rows) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(a.src + r * a.ld_src + j * 16)[q];
       if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + j * 16);
     }
-    for (; j < cpr; j += blockDim.x) {
-      const int c0 = j * 16;
-      int v[16];
+    const uint32_t grow = (uint32_t)(a.sr.row_base + cr);
+    const int8_t* mb = reinterpret_cast<const int8_t*>(&mk);
+    const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mk);
+    uint32_t packed[4];
+    int sq32 = 0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        v[4 * q] = nx[q].x; v[4 * q + 1] = nx[q].y; v[4 * q + 2] = nx[q].z; v[4 * q + 3] = nx[q].w;
-      }
-      const int4 mk = nm;
-      const int jn = j + blockDim.x;
-      if (jn < cpr) {
+    for (int q = 0; q < 4; ++q) {
+      const Philox4 rnd = sr_quad_k(a.keys, a.sr.stream, grow, (uint32_t)((c0 >> 2) + q));
+      int y4[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(srow + jn * 16)[q];
-        if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + jn * 16);
-      }
-      const int8_t* mb = reinterpret_cast<const int8_t*>(&mk);
-      uint32_t packed[4];
-      int sq32 = 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const Philox4 rnd = sr_quad(a.sr.seed, a.sr.stream, grow, (uint32_t)((c0 >> 2) + q));
-        packed[q] = 0u;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int e = 4 * q + k;
-          const int c = c0 + e;
-          int x = v[e];
-          if (BIAS) x = add32(x, a.bias[c]);
-          const i64 prod = (i64)x * (i64)(COLM ? a.mult_col[c] : mult_s);
-          const uint32_t f = quad_word(rnd, k);
-          int y;
-          if (BIG) {
-            const i64 p2 = prod + (i64)((u64)f << lo);
-            const int hi = (int)(p2 >> 32);
-            if (__funnelshift_r((uint32_t)p2, (uint32_t)hi, lo) != 0xFFFFFFFFu)
-              y = hi >> lo;  // (p2 >> shift) fits int32
-            else
-              y = (int)sr_round(prod, sh, f, a.sr.seed, a.sr.stream, grow, (uint32_t)c);
-          } else {
-            const u64 u = sh == 32 ? (u64)f : (u64)(f & ((1u << sh) - 1u));
-            const i64 t = sar64(prod + (i64)u, sh);
-            y = t < -127 ? -127 : (t > 127 ? 127 : (int)t);
-          }
-          y = y < -127 ? -127 : (y > 127 ? 127 : y);
-          if (a.relu && y < 0) y = 0;
-          if (MASK && mb[e] <= 0) y = 0;
-          if (SUMSQ) sq32 += y * y;
-          packed[q] |= (uint32_t)(uint8_t)(int8_t)y << (8 * k);
+      for (int k = 0; k < 4; ++k) {
+        const int e = 4 * q + k;
+        const int c = c0 + e;
+        int x = v[e];
+        if (BIAS) x = add32(x, a.bias[c]);
+        const i64 prod = mul_wide_s32(x, COLM ? a.mult_col[c] : mult_s);
+        const uint32_t f = quad_word(rnd, k);
+        int y;
+        if (BIG) {
+          const i64 p2 = mad_wide_u32(f, pow2lo, prod);  // prod + (f << lo)
+          if (__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) != 0xFFFFFFFFu)
+            y = hi32(p2) >> lo;  // (p2 >> shift) fits int32
+          else
+            y = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, f, a.sr.seed, a.sr.stream, grow,
+                                                           (uint32_t)c)));
+        } else {
+          const u64 u = sh == 32 ? (u64)f : (u64)(f & ((1u << sh) - 1u));
+          const i64 t = sar64(prod + (i64)u, sh);
+          y = t < -128 ? -128 : (t > 128 ? 128 : (int)t);
         }
+        y = max(min(y, 127), lower);  // saturate, ReLU
+        if (MASK && SUMSQ && mb[e] <= 0) y = 0;
+        if (SUMSQ) sq32 += y * y;
+        y4[k] = y;
       }
-      if (SUMSQ) sq += sq32;
-      *reinterpret_cast<int4*>(drow + c0) = make_int4(packed[0], packed[1], packed[2], packed[3]);
+      packed[q] = pack4(y4[0], y4[1], y4[2], y4[3]);
+      if (MASK && !SUMSQ) packed[q] &= bytes_positive(mw[q]);
     }
+    if (SUMSQ) sq += sq32;
+    *reinterpret_cast<int4*>(a.dst + cr * a.ld_dst + c0) = make_int4(packed[0], packed[1], packed[2], packed[3]);
   }
   if (SUMSQ) block_reduce_to<false>(sq, a.sumsq);
 }
@@ -313,7 +326,7 @@ extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols
   if (rows == 0 || cols == 0) return ECO_OK;
   RequantArgs a{src, rows, cols, ld_src, bias_col, mult_col, mult_scalar, shift, relu, sr,
                 mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq),
-                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX};
+                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX, philox_keys(sr.seed)};
   const bool replay = sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64;
   const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
                    ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0)) &&
