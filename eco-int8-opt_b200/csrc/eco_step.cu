@@ -65,7 +65,7 @@ ECO_DEV int shift_of(double r, unsigned& flags) {
 ECO_DEV LayerScalars layer_scalars(const eco_i8eco_layer_t& L, const eco_i8eco_hyper_t& H) {
   LayerScalars S;
   S.flags = 0;
-  double s_g = L.s_g;
+  double s_g = L.s_g_dev ? __longlong_as_double(*L.s_g_dev) : L.s_g;
   if (H.grad_clip >= 0.0) {  // iopt.py:90-101
     const i64 sq = *L.gsq;
     const double n_real = __dmul_rn(__dsqrt_rn(__ll2double_rn(sq)), s_g);
@@ -77,7 +77,7 @@ ECO_DEV LayerScalars layer_scalars(const eco_i8eco_layer_t& L, const eco_i8eco_h
   S.com_m = shift_of(__ddiv_rn(S.sm4096, L.sw_min), S.flags);
   S.com_g = shift_of(__ddiv_rn(S.sg4096, L.sw_min), S.flags);
   S.com_mm = S.s_m > 0.0 ? shift_of(__ddiv_rn(__ddiv_rn(L.sw_max, 4096.0), S.s_m), S.flags) : 0;
-  S.lr_sgb = __dmul_rn(H.lr, L.s_gb);
+  S.lr_sgb = __dmul_rn(H.lr, L.s_gb_dev ? __longlong_as_double(*L.s_gb_dev) : L.s_gb);
   S.com_b = L.b_acc ? shift_of(__ddiv_rn(S.lr_sgb, __dmul_rn(L.sx, L.sw_min)), S.flags) : 0;
   if (S.com_m > 62 || S.com_g > 62 || S.com_mm > 62 || S.com_b > 62) S.flags |= ECO_FLAG_SHIFT_OVERFLOW;
   return S;

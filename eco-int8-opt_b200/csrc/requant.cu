@@ -73,6 +73,8 @@ struct RequantArgs {
   i64* sumsq;
   int mult32;  // mult_scalar fits int32: 32x32->64 products
   PhiloxKeys keys;  // round keys of sr.seed (Philox mode)
+  const i64* dparams;  // nullable: [_, mult, shift] on the device (eco_scale_from_amax) replace
+                       // mult_scalar and shift; a shift beyond 62 stores zeros (already flagged)
 };
 
 // MODE: 0 round half up, 1 Philox, 2 replay.  One thread handles 16 consecutive
@@ -81,7 +83,11 @@ template <bool VEC, int MODE>
 __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) {
   const i64 cpr = (a.cols + 15) / 16;
   const i64 total = a.rows * cpr;
-  const bool left = a.shift < 0;
+  const int shift = a.dparams ? (int)a.dparams[2] : a.shift;
+  const i64 mult_scalar = a.dparams ? a.dparams[1] : a.mult_scalar;
+  const bool mult32 = a.dparams ? true : a.mult32;
+  const bool zero_out = shift > 62;
+  const bool left = shift < 0;
   i64 sq = 0;
   for (i64 t = (i64)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (i64)gridDim.x * blockDim.x) {
     const i64 r = t / cpr;
@@ -102,8 +108,8 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       Philox4 rnd{0u, 0u, 0u, 0u};
-      if (MODE == 1 && !left)
-        rnd = sr_quad(a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)((c0 >> 2) + q));
+      if (MODE == 1 && !left && !zero_out)
+        rnd = sr_quad_k(a.keys, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)((c0 >> 2) + q));
       packed[q] = 0u;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -113,17 +119,19 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
         int x = v[e];
         if (a.bias && in) x = add32(x, a.bias[c]);
         const i64 prod = a.mult_col ? (i64)x * (i64)(in ? a.mult_col[c] : 0)
-                                    : (a.mult32 ? (i64)x * (i64)(int)a.mult_scalar : mul64((i64)x, a.mult_scalar));
+                                    : (mult32 ? (i64)x * (i64)(int)mult_scalar : mul64((i64)x, mult_scalar));
         i64 yv;
-        if (left)
-          yv = shl64(prod, -a.shift);
+        if (zero_out)
+          yv = 0;
+        else if (left)
+          yv = shl64(prod, -shift);
         else if (MODE == 0)
-          yv = sar64(add64(prod, half_nudge(a.shift)), a.shift);
+          yv = sar64(add64(prod, half_nudge(shift)), shift);
         else if (MODE == 1)
-          yv = sr_round(prod, a.shift, quad_word(rnd, k), a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r),
+          yv = sr_round(prod, shift, quad_word(rnd, k), a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r),
                         (uint32_t)c);
         else
-          yv = in ? sar64(add64(prod, replay_nudge(a.sr, r, c)), a.shift) : 0;
+          yv = in ? sar64(add64(prod, replay_nudge(a.sr, r, c)), shift) : 0;
         int8_t y = sat8(yv);
         if (a.relu && y < 0) y = 0;
         if (a.mask && in && a.mask[r * a.ld_mask + c] <= 0) y = 0;
@@ -152,11 +160,15 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
 template <bool MASK, bool SUMSQ, bool COLM, bool BIAS, bool BIG>
 __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantArgs a) {
   const int cpr = (int)(a.cols >> 4);
-  const int sh = a.shift;
+  const int sh = a.dparams ? (int)a.dparams[2] : a.shift;
+  // with device parameters both variants are launched and the one that does not
+  // match the shift returns; a shift beyond 62 or below 0 is the small variant's
+  if (a.dparams && BIG != (sh > 32 && sh <= 62)) return;
+  const bool zero_out = sh > 62;
   const int lo = sh - 32;  // BIG: bits of the tie-break draw
   const uint32_t pow2lo = BIG ? 1u << lo : 0u;
   const int lower = a.relu ? 0 : -127;
-  const int32_t mult_s = (int32_t)a.mult_scalar;
+  const int32_t mult_s = (int32_t)(a.dparams ? a.dparams[1] : a.mult_scalar);
   long long sq = 0;
   // The block's work is the chunk sequence (row r, chunk j) with rows blockIdx.x +
   // k * gridDim.x; thread t takes every blockDim.x-th chunk of it, and the next
@@ -217,10 +229,15 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
           else
             y = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, f, a.sr.seed, a.sr.stream, grow,
                                                            (uint32_t)c)));
-        } else {
+        } else if (sh >= 0 && !zero_out) {
           const u64 u = sh == 32 ? (u64)f : (u64)(f & ((1u << sh) - 1u));
           const i64 t = sar64(prod + (i64)u, sh);
           y = t < -128 ? -128 : (t > 128 ? 128 : (int)t);
+        } else if (!zero_out) {  // left shift: no draw
+          const i64 t = shl64(prod, -sh);
+          y = t < -128 ? -128 : (t > 128 ? 128 : (int)t);
+        } else {
+          y = 0;
         }
         y = max(min(y, 127), lower);  // saturate, ReLU
         if (MASK && SUMSQ && mb[e] <= 0) y = 0;
@@ -312,6 +329,45 @@ int grid_for(i64 work, int per_sm = 8) {
 
 }  // namespace
 
+// dX / dW requant whose scalar multiplier and shift were computed on the device
+// (eco_scale_from_amax); Philox stochastic rounding only.
+extern "C" int eco_requant_s32_s8_dev(const int32_t* src, int64_t rows, int64_t cols, int64_t ld_src,
+                                      const int64_t* params, int relu, eco_sr_t sr, const int8_t* mask,
+                                      int64_t ld_mask, int8_t* dst, int64_t ld_dst, int64_t* sumsq,
+                                      eco_stream_t stream) {
+  ECO_REQUIRE(src && dst && params && rows >= 0 && cols >= 0 && ld_src >= cols && ld_dst >= cols, ECO_ERR_ARG,
+              "eco_requant_s32_s8_dev: bad arguments");
+  ECO_REQUIRE(!mask || ld_mask >= cols, ECO_ERR_ARG, "eco_requant_s32_s8_dev: bad mask leading dim");
+  ECO_REQUIRE(sr.mode == ECO_SR_PHILOX, ECO_ERR_ARG, "eco_requant_s32_s8_dev: Philox rounding only");
+  cudaStream_t s = eco_stream(stream);
+  if (sumsq && cudaMemsetAsync(sumsq, 0, sizeof(int64_t), s) != cudaSuccess)
+    return eco_launch_check("eco_requant_s32_s8_dev memset");
+  if (rows == 0 || cols == 0) return ECO_OK;
+  RequantArgs a{src, rows, cols, ld_src, nullptr, nullptr, 0, 0, relu, sr,
+                mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq), 1, philox_keys(sr.seed),
+                reinterpret_cast<const i64*>(params)};
+  const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
+                   ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0));
+  if (vec) {
+    const int gp = (int)std::max<i64>(1, std::min<i64>(rows, (i64)eco_num_sms() * 8));
+#define ECO_RQD(M, Q)                                                                   \
+  do {                                                                                  \
+    requant_philox_kernel<M, Q, false, false, true><<<gp, kThreads, 0, s>>>(a);         \
+    requant_philox_kernel<M, Q, false, false, false><<<gp, kThreads, 0, s>>>(a);        \
+  } while (0)
+    if (mask) {
+      if (sumsq) ECO_RQD(true, true); else ECO_RQD(true, false);
+    } else {
+      if (sumsq) ECO_RQD(false, true); else ECO_RQD(false, false);
+    }
+#undef ECO_RQD
+    return eco_launch_check("eco_requant_s32_s8_dev");
+  }
+  const int g = grid_for(rows * ((cols + 15) / 16));
+  requant_kernel<false, 1><<<g, kThreads, 0, s>>>(a);
+  return eco_launch_check("eco_requant_s32_s8_dev");
+}
+
 extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols, int64_t ld_src,
                                   const int32_t* bias_col, const int32_t* mult_col, int64_t mult_scalar,
                                   int shift, int relu, eco_sr_t sr, const int8_t* mask, int64_t ld_mask,
@@ -326,7 +382,7 @@ extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols
   if (rows == 0 || cols == 0) return ECO_OK;
   RequantArgs a{src, rows, cols, ld_src, bias_col, mult_col, mult_scalar, shift, relu, sr,
                 mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq),
-                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX, philox_keys(sr.seed)};
+                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX, philox_keys(sr.seed), nullptr};
   const bool replay = sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64;
   const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
                    ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0)) &&

@@ -38,7 +38,8 @@ class I8ECOLayer(ctypes.Structure):
                 ("b_acc", c_p), ("gb_sum", c_p), ("nudge_w", c_p), ("nudge_m", c_p), ("nudge_b", c_p),
                 ("rows", c_i64), ("cols", c_i64), ("row_base", c_i64), ("sw_min", c_d), ("sw_max", c_d), ("s_g", c_d),
                 ("s_gb", c_d), ("sx", c_d), ("stream_w", c_u64), ("stream_b", c_u64),
-                ("nudge_m_bits", c_i32), ("nudge_b_bits", c_i32), ("bias_rows", c_i64)]
+                ("nudge_m_bits", c_i32), ("nudge_b_bits", c_i32), ("bias_rows", c_i64),
+                ("s_g_dev", c_p), ("s_gb_dev", c_p)]
 
 
 class I8ECOHyper(ctypes.Structure):
@@ -59,6 +60,9 @@ _SIGS = {
                                        c_p, c_p]),
     "eco_set_gemm_sm_limit": (c_i32, [c_i32]),
     "eco_split_cols_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_i64, c_p, c_p]),
+    "eco_scale_from_amax": (c_i32, [c_p, c_i32, c_p, c_d, c_d, c_p, c_p, c_p]),
+    "eco_requant_s32_s8_dev": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, SRSpec, c_p, c_i64, c_p, c_i64, c_p,
+                                       c_p]),
     "eco_peer_push_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, c_i64, c_i64, c_i32, c_i32, c_p]),
     "eco_peer_signal": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i64, c_p]),
     "eco_peer_wait": (c_i32, [c_p, c_i32, c_i32, c_i64, c_i64, c_p]),

@@ -82,6 +82,24 @@ def requant(src: torch.Tensor, mult, shift: int, site: Site, bias: torch.Tensor 
     return dst
 
 
+def requant_dev(src: torch.Tensor, scale, key: int, row_base: int, mask: torch.Tensor | None = None,
+                sumsq: torch.Tensor | None = None) -> torch.Tensor:
+    """int32 [R,C] -> int8 with the multiplier and shift of a device scale
+    (``_scale.DevScale``), Philox rounding with site key ``key``."""
+    nat.require_cuda(src, mask, sumsq)
+    src = _rowmajor(src)
+    rows, cols = src.shape
+    ld_mask = 0
+    if mask is not None:
+        mask = _rowmajor(mask)
+        ld_mask = mask.stride(0) if rows > 1 else cols
+    dst = torch.empty((rows, cols), dtype=_I8, device=src.device)
+    spec = nat.sr_spec(nat.SR_PHILOX, seed=key, stream_id=0, row_base=row_base)
+    nat.call("eco_requant_s32_s8_dev", src.data_ptr(), rows, cols, src.stride(0) if rows > 1 else cols,
+             scale.t.data_ptr(), 0, spec, nat.ptr(mask), ld_mask, dst.data_ptr(), cols, nat.ptr(sumsq), nat.stream())
+    return dst
+
+
 def apply_mult_shift(x: torch.Tensor, mult, mult_kind: int, shift: int, site: Site) -> torch.Tensor:
     """int64 ``apply_mult_shift`` over a contiguous [rows, cols] view of ``x``."""
     nat.require_cuda(x, mult if isinstance(mult, torch.Tensor) else None)

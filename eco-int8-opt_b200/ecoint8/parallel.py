@@ -166,7 +166,7 @@ def start_dw_reduction(layer, dw_acc: torch.Tensor, gb_sum: torch.Tensor, s_g: f
         red = torch.empty((hi - lo, dw_acc.shape[1]), dtype=dw_acc.dtype, device=dw_acc.device)
         work = dist.reduce_scatter_tensor(red, dw_acc, op=dist.ReduceOp.SUM, group=_GROUP, async_op=True)
     layer._dw_pending = {"red": red, "full": dw_acc, "shape": tuple(dw_acc.shape), "work": work, "gb": gb_sum,
-                         "rows": rows, "s_g": float(s_g)}
+                         "rows": rows, "s_g": s_g}
     _PENDING.append(layer)
 
 
@@ -257,7 +257,7 @@ def start_dw_rows_peer(layer, g_i8: torch.Tensor, s_g: float) -> None:
         done = torch.cuda.Event()
         done.record(dws)
     layer._dw_pending = {"red": red, "full": None, "shape": (bufs.out, bufs.in_f), "work": None, "gb": None,
-                         "gb_rows": gb_rows, "event": done, "rows": (lo, hi), "s_g": float(s_g), "amax": amax}
+                         "gb_rows": gb_rows, "event": done, "rows": (lo, hi), "s_g": s_g, "amax": amax}
     _PENDING.append(layer)
 
 
@@ -275,7 +275,7 @@ def start_dw_rows(layer, dy_cols: torch.Tensor, a2a, s_g: float) -> None:
     gb = torch.zeros(out, dtype=torch.int64, device=red.device)
     gb[lo:hi] = _ops.colsum(dy_cols)  # the other rows arrive through the flat SUM in finalize_pending
     layer._dw_pending = {"red": red, "full": None, "shape": (out, in_f), "work": None, "gb": gb,
-                         "rows": (lo, hi), "s_g": float(s_g), "amax": amax}
+                         "rows": (lo, hi), "s_g": s_g, "amax": amax}
     _PENDING.append(layer)
 
 
@@ -332,9 +332,14 @@ def finalize_pending() -> None:
                             for l, a in zip(layers, fused)])
     dist.all_reduce(maxima, op=dist.ReduceOp.MAX, group=_SMALL)
     sumsq = torch.zeros(len(layers), dtype=torch.int64, device=dev)
-    for i, (layer, a_dw) in enumerate(zip(layers, maxima.tolist())):
+    queued = [bool(l._dw_pending.get("queued")) for l in layers]
+    host = None if all(queued) else maxima.tolist()  # a queued backward keeps the maxima on the device
+    for i, layer in enumerate(layers):
         replicated = layer._dw_pending["rows"] is None
-        layer._finalize_dw(int(a_dw), sumsq[i:i + 1])
+        if queued[i]:
+            layer._finalize_dw_queued(maxima[i:i + 1], sumsq[i:i + 1])
+        else:
+            layer._finalize_dw(int(host[i]), sumsq[i:i + 1])
         if replicated and rank() != 0:  # every rank holds the whole layer: count it once
             sumsq[i:i + 1].zero_()
     dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=_SMALL)

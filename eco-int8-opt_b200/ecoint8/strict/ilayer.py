@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from .. import _native, _ops, _sr, parallel
+from .. import _native, _ops, _scale, _sr, parallel
 from ..fixedpoint import (
     _check_int,
     _check_shift,
@@ -176,8 +176,13 @@ class I8Linear(nn.Module):
 
     _gw_i8 = property(lambda self: self._grad_get("_gw_i8"),
                       lambda self, v: self.__dict__.__setitem__("_gw_i8_store", v))
-    _gw_s = property(lambda self: self._grad_get("_gw_s"),
+    _gw_s = property(lambda self: _scale.as_float(self._grad_get("_gw_s")) if self._grad_get("_gw_s") is not None
+                     else None,
                      lambda self, v: self.__dict__.__setitem__("_gw_s_store", v))
+    # the bias gradient's scale (ilayer.py:169); a device scale while a queued backward runs
+    _gb_s = property(lambda self: _scale.as_float(self.__dict__["_gb_s_store"])
+                     if self.__dict__.get("_gb_s_store") is not None else None,
+                     lambda self, v: self.__dict__.__setitem__("_gb_s_store", v))
     _gb_sum = property(lambda self: self._grad_get("_gb_sum"),
                        lambda self, v: self.__dict__.__setitem__("_gb_sum_store", v))
 
@@ -330,7 +335,37 @@ class I8Linear(nn.Module):
         requant_dw(rd_dw.value()[0])
         return dx_i8, s_dx
 
-    def _backward_dp(self, g_i8, s_g, x_i8, mask, dev):
+    def _backward_queued(self, g_i8: torch.Tensor, s_g, _mask: torch.Tensor | None = None):
+        """``backward_i8`` for a pass queued without host round trips (Philox mode):
+        ``s_g`` is a float or a device scale, the dX and dW scales are computed on the
+        device (``_scale``) and the returned ``s_dx`` is a device scale.  Same keys,
+        draws and results as ``backward_i8``."""
+        _check_int(g_i8, "grad output")
+        assert self._cache_x is not None, "call forward_i8 before backward_i8"
+        x_i8 = self._cache_x
+        assert isinstance(self.sx, float)
+        dev = _native.require_cuda(g_i8, x_i8, self.w_i8)
+        N, out = g_i8.shape
+        in_f = x_i8.shape[1]
+        if parallel.active():
+            return self._backward_dp(g_i8, s_g, x_i8, _mask, dev, queued=True)
+        amax = torch.empty(2, dtype=torch.int32, device=dev)
+        dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax[1:2])
+        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N, amax=amax[0:1])
+        self._gb_sum = _ops.colsum(g_i8)
+        self._gb_s = s_g
+        key_w = _sr.reserve_key()  # the dW site's key, then the dX site's (the reference's order)
+        s_dx = _scale.from_amax(amax[1:2], s_g, self._sw_mean())
+        dx_i8 = _ops.requant_dev(dx_acc, s_dx, _sr.new_key(), _sr.row_base(), mask=_mask)
+        s_gw = _scale.from_amax(amax[0:1], s_g, self.sx)
+        self._gw_sumsq = torch.empty(1, dtype=torch.int64, device=dev)
+        self._gw_i8 = _ops.requant_dev(dw_acc, s_gw, key_w, 0, sumsq=self._gw_sumsq)
+        self._gw_sumsq_of = self._gw_i8
+        self._gw_s = s_gw
+        self._gw_rows = None
+        return dx_i8, s_dx
+
+    def _backward_dp(self, g_i8, s_g, x_i8, mask, dev, queued: bool = False):
         """Data-parallel backward: dW rows formed asynchronously (reduce-scatter of the
         int32 accumulators, or one GEMM over the gathered global batch) and finalized
         when the gradient is read; global dX maximum over ranks; dX requant.  Same
@@ -352,10 +387,18 @@ class I8Linear(nn.Module):
         elif not gathered:
             parallel.start_dw_reduction(self, dw_acc, gb_sum, s_g)
             self._dw_pending["key"] = key_w
-        self._gb_s = float(s_g)
+        self._gb_s = s_g
         amax_dx = torch.empty(1, dtype=torch.int32, device=dev)
         dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax_dx)
         t, work = parallel.start_max(amax_dx)
+        if queued:  # the dX scale from the global maximum, on the device
+            if gathered:
+                parallel.start_dw_rows(self, dy_cols, a2a, s_g)
+                self._dw_pending["key"] = key_w
+            self._dw_pending["queued"] = True
+            work.wait()
+            s_dx = _scale.from_amax(t, s_g, self._sw_mean())
+            return _ops.requant_dev(dx_acc, s_dx, _sr.new_key(), _sr.row_base(), mask=mask), s_dx
         rd_dx = _ops.read_later(t, work)
         if gathered:  # the dW GEMM runs while the host waits for the dX maximum
             parallel.start_dw_rows(self, dy_cols, a2a, s_g)
@@ -369,6 +412,17 @@ class I8Linear(nn.Module):
         site = _requant_site((N, in_f), sh_dx, dev, True, "dx")
         dx_i8 = _ops.requant(dx_acc, m_dx, sh_dx, site, mask=mask)
         return dx_i8, s_dx
+
+    def _finalize_dw_queued(self, amax: torch.Tensor, sumsq_out: torch.Tensor) -> None:
+        """``_finalize_dw`` with the global maximum on the device (a queued backward)."""
+        p = self.__dict__["_dw_pending"]
+        self._dw_pending = None
+        s_gw = _scale.from_amax(amax, p["s_g"], self.sx)
+        rows = p["rows"]
+        self._gw_i8 = _ops.requant_dev(p["red"], s_gw, p["key"], 0 if rows is None else rows[0], sumsq=sumsq_out)
+        self._gw_s = s_gw
+        self._gw_rows = rows
+        self._gb_sum = p["gb"]
 
     def _finalize_dw(self, a_dw: int, sumsq_out: torch.Tensor) -> None:
         """Requantize this rank's rows of the summed dW with the global maximum."""
@@ -496,16 +550,20 @@ class I8Sequential(nn.Module):
         """Explicit reverse pass (ilayer.py:238-245); a ReLU mask rides in the dX requant."""
         _check_int(g_i8, "net grad")
         blocks = list(self.blocks)
+        # Philox mode queues the whole pass: scales stay on the device between layers
+        # (the per-layer site log and the replay mode need host shifts: layer by layer)
+        queued = not _sr.replaying() and _sr.LOG is None and g_i8.is_cuda
         i = len(blocks) - 1
         while i >= 0:
             blk = blocks[i]
             if isinstance(blk, I8Linear):
+                step = blk._backward_queued if queued else blk.backward_i8
                 prev = blocks[i - 1] if i > 0 else None
                 if isinstance(prev, I8ReLU) and prev._mask_source() is not None:
-                    g_i8, s_g = blk.backward_i8(g_i8, s_g, _mask=prev._mask_source())
+                    g_i8, s_g = step(g_i8, s_g, _mask=prev._mask_source())
                     i -= 2
                     continue
-                g_i8, s_g = blk.backward_i8(g_i8, s_g)
+                g_i8, s_g = step(g_i8, s_g)
             elif isinstance(blk, I8ReLU):
                 g_i8 = blk.backward_mask(g_i8)
             i -= 1

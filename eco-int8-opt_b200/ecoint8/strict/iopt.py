@@ -35,7 +35,7 @@ import struct
 import torch
 
 from .. import _native as nat
-from .. import _ops, _sr, parallel
+from .. import _ops, _scale, _sr, parallel
 from ..fixedpoint import _check_int, quantize_multiplier
 from .ilayer import _ScaleList
 
@@ -162,11 +162,13 @@ class I8ECO:
     def _raise_pending(self, block: bool) -> None:
         if self._err is None:
             return
-        event, flags = self._err
+        event, flags, sflags = self._err
         if not block and not event.query():
             return
         event.synchronize()
         self._err = None
+        if int(sflags[0]):  # a device scale of the queued backward overflowed (the reference raises there)
+            _scale.raise_flags(self._state.device)
         bad = [(i, int(f)) for i, f in enumerate(flags.tolist()) if f]
         if bad:
             self._state[:, 2].zero_()
@@ -215,24 +217,35 @@ class I8ECO:
                 raise RuntimeError("I8ECO: weights, momentum and gradient must be contiguous int8 of one shape")
             nat.require_cuda(g)
             out, rowlen = w.shape
-            s_g = float(layer._gw_s)
+            s_g_raw = layer.__dict__.get("_gw_s_store")  # a float, or a device scale of a queued backward
+            queued_g = isinstance(s_g_raw, _scale.DevScale) and not replay
+            s_g = 0.0 if queued_g else _scale.as_float(s_g_raw)
             gsq = self._gsq(layer, g) if self.grad_clip is not None else None
             d.g, d.gsq, d.s_g = g.data_ptr(), nat.ptr(gsq), s_g
+            d.s_g_dev = s_g_raw.ptr() if queued_g else None
+            d.s_gb_dev = None
             d.nudge_w = d.nudge_m = d.nudge_b = None
             d.nudge_m_bits = d.nudge_b_bits = 32
             if layer.use_bias:
                 gb = layer._gb_sum
                 if gb.dtype != torch.int64 or gb.device != dev or not gb.is_contiguous():
                     gb = gb.to(device=dev, dtype=torch.int64).contiguous()
-                s_gb = float(layer._gb_s)
-                com_b = _common_shift([self.lr * s_gb / (layer.sx * d.sw_min)])  # = min over rows
-                if com_b > 62:  # the reference's torch.randint(0, 2**com_b) raises (iopt.py:194)
-                    raise ValueError("Overflow when unpacking long long")
-                d.gb_sum, d.s_gb = gb.data_ptr() + 8 * lo, s_gb
+                s_gb_raw = layer.__dict__.get("_gb_s_store")
+                if isinstance(s_gb_raw, _scale.DevScale) and not replay:
+                    # on the device: the kernel flags a bias shift beyond 62 and leaves the layer
+                    d.s_gb, d.s_gb_dev = 0.0, s_gb_raw.ptr()
+                    keep.append(s_gb_raw.t)
+                else:
+                    s_gb = _scale.as_float(s_gb_raw)
+                    com_b = _common_shift([self.lr * s_gb / (layer.sx * d.sw_min)])  # = min over rows
+                    if com_b > 62:  # the reference's torch.randint(0, 2**com_b) raises (iopt.py:194)
+                        raise ValueError("Overflow when unpacking long long")
+                    d.s_gb = s_gb
+                d.gb_sum = gb.data_ptr() + 8 * lo
                 keep.append(gb)
             if replay:
                 keep += self._replay_nudges(d, layer, s_m_now[i], s_g, gsq, (out, rowlen), lo)
-            keep += [g, gsq]
+            keep += [g, gsq] + ([s_g_raw.t] if queued_g else [])
         hyper = nat.I8ECOHyper()
         hyper.lr = self.lr
         hyper.grad_clip = -1.0 if self.grad_clip is None else float(self.grad_clip)
@@ -260,14 +273,16 @@ class I8ECO:
         # (allocating pinned memory every step can stall the host)
         if getattr(self, "_flag_bufs", None) is None or self._flag_bufs[0][0].numel() != len(self.layers):
             self._flag_bufs = [(torch.empty(len(self.layers), dtype=torch.int64, pin_memory=True),
+                                torch.empty(1, dtype=torch.int32, pin_memory=True),
                                 torch.cuda.Event()) for _ in range(2)]
             self._flag_turn = 0
-        flags, ev = self._flag_bufs[self._flag_turn]
+        flags, sflags, ev = self._flag_bufs[self._flag_turn]
         self._flag_turn ^= 1
         ev.synchronize()  # its previous copy finished a step ago
         flags.copy_(self._state[:, 2], non_blocking=True)
+        sflags.copy_(_scale.flags(dev), non_blocking=True)
         ev.record()
-        self._err = (ev, flags)
+        self._err = (ev, flags, sflags)
         self._keep = keep  # released at the next step (stream-ordered reuse is safe)
 
     def _plan(self, active, dev, dp):
@@ -359,7 +374,8 @@ class I8ECO:
         d.nudge_m = nm.data_ptr() + (d.nudge_m_bits // 8) * lo * rowlen if ms else nm.data_ptr()
         kept = [nw, nm]
         if layer.use_bias:
-            com_b = _common_shift([self.lr * float(layer._gb_s) / (layer.sx * sw_o) for sw_o in layer.sw])
+            com_b = _common_shift([self.lr * _scale.as_float(layer.__dict__.get("_gb_s_store")) / (layer.sx * sw_o)
+                                   for sw_o in layer.sw])
             if com_b >= 0:
                 nb = _sr.replay_draw((out, 1), 1 << com_b, dev).reshape(out).contiguous()
             else:

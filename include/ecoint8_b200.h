@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define ECO_ABI_VERSION 2
+#define ECO_ABI_VERSION 3
 
 enum {
   ECO_OK = 0,
@@ -156,6 +156,27 @@ ECO_API int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_
 ECO_API int eco_split_cols_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int64_t parts,
                       int8_t* dst, eco_stream_t stream);
 
+/* ---------------------------------------------- device-side scales -----
+ * The backward's dynamic scale chain without host round trips (used when a whole
+ * backward pass is queued at once): the reference's dynamic_scale_from_int and
+ * quantize_multiplier (fixedpoint.py:105-114, :26-37) in the same IEEE double
+ * arithmetic, then the requant reads the multiplier and shift from the device.
+ *
+ * eco_scale_from_amax: gain = (gain0_dev ? *gain0_dev (double bits) : gain0) * gain1;
+ * s = amax * gain / 127 (1.0 when <= 0); (mult, shift) = quantize_multiplier(gain / s).
+ * out: int64[3] = {double bits of s, mult, shift}.  A shift beyond 62 (the reference
+ * raises) or a negative / non-finite ratio ORs ECO_FLAG_SHIFT_OVERFLOW /
+ * ECO_FLAG_BAD_RATIO (1 / 2) into *flags (nullable). */
+ECO_API int eco_scale_from_amax(const void* amax, int amax_bits, const int64_t* gain0_dev, double gain0,
+                        double gain1, int64_t* out, uint32_t* flags, eco_stream_t stream);
+
+/* eco_requant_s32_s8 with a scalar multiplier and shift read from params[1], params[2]
+ * (the output of eco_scale_from_amax) and Philox rounding; no bias, no per-column
+ * multipliers.  A shift beyond 62 stores zeros (the scale kernel flagged it). */
+ECO_API int eco_requant_s32_s8_dev(const int32_t* src, int64_t rows, int64_t cols, int64_t ld_src,
+                           const int64_t* params, int relu, eco_sr_t sr, const int8_t* mask, int64_t ld_mask,
+                           int8_t* dst, int64_t ld_dst, int64_t* sumsq, eco_stream_t stream);
+
 /* ------------------------------------------ data-parallel peer exchange -----
  * No reference counterpart (the reference has no data parallelism).  The buffers
  * are allocated on every rank and mapped into each process (each rank holds
@@ -223,6 +244,9 @@ typedef struct {
                              those rows: a data-parallel row shard then updates every bias
                              (the bias step does not depend on the weights) and no rank has
                              to receive the others' biases */
+  const int64_t* s_g_dev;  /* nullable: s_g as double bits on the device (a scale computed by
+                              eco_scale_from_amax), used instead of s_g */
+  const int64_t* s_gb_dev; /* nullable: likewise for s_gb */
 } eco_i8eco_layer_t;
 
 typedef struct {

@@ -350,3 +350,39 @@ def test_sequential_fusion_equals_unfused_modules():
         yb, _ = b.blocks[2].forward_i8(h)
     assert torch.equal(ya, yb)
     assert torch.equal(a.blocks[1].mask_cache, b.blocks[1].mask_cache)
+
+
+def test_queued_backward_equals_layer_by_layer():
+    """``I8Sequential.backward_i8`` in Philox mode queues the whole pass with the scales
+    on the device; the same training run layer by layer (host scales: the site log
+    forces it) must give identical weights, momentum, biases, s_m, stats and gradient
+    scales after every step.  Widths cover the 16-aligned and the odd-width kernels."""
+    from ecoint8 import I8ECO, I8Linear, I8ReLU, I8Sequential, _sr
+
+    def run(logged):
+        torch.manual_seed(5)
+        net = I8Sequential(I8Linear(64, 256), I8ReLU(), I8Linear(256, 96), I8ReLU(), I8Linear(96, 10)).cuda()
+        gen = torch.Generator().manual_seed(9)
+        X = torch.randn(128, 64, generator=gen)
+        yl = torch.randint(0, 10, (128,), generator=gen)
+        x0, sx0 = bnd.quantize_tensor_dynamic(X)
+        net.calibrate(x0.cuda(), sx0)
+        opt = I8ECO(net.int8_layers(), lr=0.3, momentum=0.9)
+        x_i8 = net.quantize_input(X.cuda())[0]
+        trail = []
+        for _ in range(4):
+            _sr.LOG = [] if logged else None
+            logits, s_out = net.forward_i8(x_i8)
+            _, g_fp = bnd.ce_grad(logits.cpu(), s_out, yl)
+            g_i8, s_g = bnd.quantize_tensor_dynamic(g_fp, stochastic=True)
+            net.backward_i8(g_i8.cuda(), s_g)
+            trail.append([fhex(l._gw_s) for l in net.int8_layers()] + [fhex(l._gb_s) for l in net.int8_layers()])
+            opt.step()
+            opt.zero_grad()
+            _sr.LOG = None
+            trail.append([digest(l.w_i8) for l in net.int8_layers()] + [digest(m) for m in opt.m_i8]
+                         + [digest(l.b_acc) for l in net.int8_layers()] + [fhex(v) for v in opt.s_m]
+                         + [fhex(opt.stats["mean_abs_e"])])
+        return trail
+
+    assert run(False) == run(True)
