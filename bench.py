@@ -159,6 +159,9 @@ def build_mlp(device, seed=0):
     return I8Sequential(*blocks).to(device)
 
 
+HOST_BLOCKED = [0.0]  # seconds the host spent waiting in the loss boundary's read
+
+
 def loss_boundary(logits_i8, s_out, y, global_batch, world):
     """fp32 boundary of examples/i8_demo.py:56-61: CE over the global batch, SR quantization of the grad."""
     import torch.distributed as dist
@@ -172,7 +175,10 @@ def loss_boundary(logits_i8, s_out, y, global_batch, world):
     if world > 1:
         dist.all_reduce(amax, op=dist.ReduceOp.MAX)
         dist.all_reduce(loss, op=dist.ReduceOp.SUM)
-    s_g = calc_scale(amax.item())
+    t0 = time.perf_counter()
+    a = amax.item()  # the step's one host synchronisation
+    HOST_BLOCKED[0] += time.perf_counter() - t0
+    s_g = calc_scale(a)
     return loss.detach(), quantize_symmetric(g, s_g, stochastic=True), s_g
 
 
@@ -421,10 +427,14 @@ def main():
         with ClockSampler(local) as clk, counter:
             torch.cuda.synchronize()
             barrier()
+            HOST_BLOCKED[0] = 0.0
+            w0 = time.perf_counter()
             ev0.record()
             for _ in range(args.steps):
                 train_step(net, opt, x_i8, y, world)
             ev1.record()
+            host_wall = time.perf_counter() - w0
+            host_blocked = HOST_BLOCKED[0]
             torch.cuda.synchronize()
             barrier()
         ms = ev0.elapsed_time(ev1)
@@ -499,7 +509,9 @@ def main():
                           "l2": "inputs larger than L2 (1.2 GB activations + 0.55 GB weights); no flush"},
                "e2e": {"value": e2e, "unit": "steps/s", "h2d_bytes_per_step": int(x_i8.numel() + y.numel() * 8),
                        "d2h_bytes_per_step": 4},
-               "gpu_launches": launches, "clocks": clk.summary()}
+               "gpu_launches": launches, "clocks": clk.summary(),
+               "host": {"issue_ms_per_step": 1e3 * (host_wall - host_blocked) / args.steps,
+                        "blocked_ms_per_step": 1e3 * host_blocked / args.steps}}
         if world == 1 and not args.no_side:
             gm, t_fused, ops = gemm_measurements(device)
             out["gemm"] = gm

@@ -25,6 +25,12 @@ struct PushArgs {
   int8_t* dst[ECO_MAX_PEERS];
   int64_t ld_dst, dst_row0;
   int n, split;
+  // optional completion signal (eco_peer_push_signal_s8): the last CTA publishes
+  // `epoch` in entry (slot, rank) of every rank's flags
+  int64_t* flags[ECO_MAX_PEERS];
+  int n_ranks, rank, slot;
+  int64_t epoch;
+  unsigned* ticket;  // zero between launches; the last CTA resets it
 };
 
 // Broadcast: every destination receives all of src at rows dst_row0 + r.
@@ -33,6 +39,10 @@ struct PushArgs {
 // thread one unit of every row: all kRows loads are in flight before the stores,
 // so a few CTAs keep enough bytes moving to fill NVLink.  VEC: 16-byte units
 // (cols, c, ld_src, ld_dst multiples of 16 and aligned bases), else bytes.
+ECO_DEV void st_release_sys(int64_t* p, int64_t v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 constexpr int kPushThreads = 512;
 constexpr int kRows = 8;
 
@@ -66,15 +76,21 @@ __global__ void __launch_bounds__(kPushThreads) peer_push_kernel(const __grid_co
       }
     }
   }
+  if (A.ticket) {
+    __threadfence_system();  // this thread's stores are visible to every GPU
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(A.ticket, 1u) == gridDim.x - 1) {  // every CTA has fenced
+      *A.ticket = 0u;
+      asm volatile("fence.sc.sys;" ::: "memory");
+      for (int p = 0; p < A.n_ranks; ++p)
+        st_release_sys(A.flags[p] + (int64_t)A.slot * ECO_MAX_PEERS + A.rank, A.epoch);
+    }
+  }
 }
 
 struct FlagArgs {
   int64_t* peer_flags[ECO_MAX_PEERS];
 };
-
-ECO_DEV void st_release_sys(int64_t* p, int64_t v) {
-  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 ECO_DEV int64_t ld_acquire_sys(const int64_t* p) {
   int64_t v;
   asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -111,6 +127,71 @@ __global__ void peer_wait_kernel(const int64_t* flags, int n, int slot, int64_t 
   }
 }
 
+// All-reduce (MAX or SUM) of a short int64 vector through the ranks' exchange
+// buffers: every rank stores its values into area (epoch & 1, rank) of every rank's
+// buffer, fences, publishes `epoch` in flag entry (slot, rank) everywhere, waits for
+// the n entries of its own slot, and reduces the n areas of its own buffer.  Two
+// areas alternate: a rank can only write an area again after a later call has seen
+// every rank's flag, i.e. after every rank finished reading it.
+struct AllreduceArgs {
+  const void* src;
+  int src_bits, count, stride, op, n, rank, slot;
+  int64_t epoch;
+  int64_t* bufs[ECO_MAX_PEERS];
+  int64_t* flags[ECO_MAX_PEERS];
+  const int64_t* own_buf;
+  const int64_t* own_flags;
+  int64_t* out;
+  unsigned long long limit_ns;
+};
+
+ECO_DEV int64_t ld_relaxed_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_constant__ AllreduceArgs A) {
+  const int par = (int)(A.epoch & 1);
+  for (int e = threadIdx.x; e < A.count; e += blockDim.x) {
+    const int64_t v = A.src_bits == 32 ? (int64_t) static_cast<const int32_t*>(A.src)[e]
+                                       : static_cast<const int64_t*>(A.src)[e];
+    for (int p = 0; p < A.n; ++p) A.bufs[p][((int64_t)par * A.n + A.rank) * A.stride + e] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < A.n) {
+    asm volatile("fence.sc.sys;" ::: "memory");
+    st_release_sys(A.flags[threadIdx.x] + (int64_t)A.slot * ECO_MAX_PEERS + A.rank, A.epoch);
+  }
+  __shared__ int s_late;
+  if (threadIdx.x == 0) s_late = 0;
+  __syncthreads();
+  if (threadIdx.x < A.n) {
+    const int64_t* f = A.own_flags + (int64_t)A.slot * ECO_MAX_PEERS + threadIdx.x;
+    if (ld_acquire_sys(f) < A.epoch) {
+      const unsigned long long t0 = peer_clock();
+      while (ld_acquire_sys(f) < A.epoch) {
+        if (peer_clock() - t0 > A.limit_ns) {
+          atomicOr(&g_peer_errors, ECO_FLAG_WAIT_TIMEOUT);
+          s_late = 1;
+          break;
+        }
+        __nanosleep(200);
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < A.count; e += blockDim.x) {
+    int64_t acc = ld_relaxed_sys(A.own_buf + (int64_t)par * A.n * A.stride + e);
+    for (int r = 1; r < A.n; ++r) {
+      const int64_t v = ld_relaxed_sys(A.own_buf + ((int64_t)par * A.n + r) * A.stride + e);
+      acc = A.op == 0 ? (v > acc ? v : acc) : (int64_t)((uint64_t)acc + (uint64_t)v);
+    }
+    A.out[e] = s_late ? 0 : acc;
+  }
+}
+
 }  // namespace
 
 // Sticky flags of the peer waits, cleared by the read (used by eco_read_device_errors).
@@ -122,17 +203,18 @@ int eco_peer_errors_take(unsigned* out) {
   return ECO_OK;
 }
 
-extern "C" int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst,
-                                int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas,
-                                eco_stream_t stream) {
+static int peer_push(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst, int n_dst,
+                     int64_t ld_dst, int64_t dst_row0, int split, int ctas, int64_t* const* peer_flags, int n_ranks,
+                     int rank, int slot, int64_t epoch, unsigned* ticket, eco_stream_t stream) {
   ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && ld_src >= cols && dst_row0 >= 0, ECO_ERR_ARG,
               "eco_peer_push_s8: bad arguments");
   ECO_REQUIRE(n_dst >= 1 && n_dst <= ECO_MAX_PEERS, ECO_ERR_ARG, "eco_peer_push_s8: 1..%d destinations",
               ECO_MAX_PEERS);
   ECO_REQUIRE(!split || cols % n_dst == 0, ECO_ERR_ARG, "eco_peer_push_s8: split needs cols divisible by n_dst");
   ECO_REQUIRE(ld_dst >= (split ? cols / n_dst : cols), ECO_ERR_ARG, "eco_peer_push_s8: ld_dst too small");
-  if (rows == 0 || cols == 0) return ECO_OK;
-  PushArgs A;
+  if ((rows == 0 || cols == 0) && !ticket) return ECO_OK;
+  ECO_REQUIRE(rows > 0 && cols > 0, ECO_ERR_ARG, "eco_peer_push_signal_s8: empty matrix");
+  PushArgs A{};
   A.src = src;
   A.ld_src = ld_src;
   A.rows = rows;
@@ -151,12 +233,42 @@ extern "C" int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows,
     }
   }
   ECO_REQUIRE(cols < (1ll << 31), ECO_ERR_ARG, "eco_peer_push_s8: too many columns");
+  A.ticket = ticket;
+  if (ticket) {
+    ECO_REQUIRE(peer_flags && n_ranks >= 1 && n_ranks <= ECO_MAX_PEERS && rank >= 0 && rank < n_ranks &&
+                    slot >= 0 && epoch > 0,
+                ECO_ERR_ARG, "eco_peer_push_signal_s8: bad signal arguments");
+    for (int p = 0; p < n_ranks; ++p) {
+      ECO_REQUIRE(peer_flags[p], ECO_ERR_ARG, "eco_peer_push_signal_s8: null flag array %d", p);
+      A.flags[p] = peer_flags[p];
+    }
+    A.n_ranks = n_ranks;
+    A.rank = rank;
+    A.slot = slot;
+    A.epoch = epoch;
+  }
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(rows, ctas > 0 ? ctas : eco_num_sms()));
   if (vec)
     peer_push_kernel<true><<<(unsigned)grid, kPushThreads, 0, eco_stream(stream)>>>(A);
   else
     peer_push_kernel<false><<<(unsigned)grid, kPushThreads, 0, eco_stream(stream)>>>(A);
   return eco_launch_check("eco_peer_push_s8");
+}
+
+extern "C" int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst,
+                                int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas,
+                                eco_stream_t stream) {
+  return peer_push(src, ld_src, rows, cols, dst, n_dst, ld_dst, dst_row0, split, ctas, nullptr, 0, 0, 0, 0, nullptr,
+                   stream);
+}
+
+extern "C" int eco_peer_push_signal_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols,
+                                       int8_t* const* dst, int n_dst, int64_t ld_dst, int64_t dst_row0, int split,
+                                       int ctas, int64_t* const* peer_flags, int n_ranks, int rank, int slot,
+                                       int64_t epoch, uint32_t* ticket, eco_stream_t stream) {
+  ECO_REQUIRE(ticket, ECO_ERR_ARG, "eco_peer_push_signal_s8: ticket word required");
+  return peer_push(src, ld_src, rows, cols, dst, n_dst, ld_dst, dst_row0, split, ctas, peer_flags, n_ranks, rank,
+                   slot, epoch, ticket, stream);
 }
 
 extern "C" int eco_peer_signal(int64_t* const* peer_flags, int n, int rank, int slot, int64_t epoch,
@@ -181,4 +293,35 @@ extern "C" int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoc
                                                   : kPeerWaitNs;
   peer_wait_kernel<<<1, 32, 0, eco_stream(stream)>>>(flags, n, slot, epoch, limit);
   return eco_launch_check("eco_peer_wait");
+}
+
+extern "C" int eco_peer_allreduce_i64(const void* src, int src_bits, int count, int op, int64_t* const* bufs,
+                                      int stride, const int64_t* own_buf, int64_t* const* peer_flags,
+                                      const int64_t* own_flags, int n, int rank, int slot, int64_t epoch,
+                                      int64_t* out, eco_stream_t stream) {
+  ECO_REQUIRE(src && bufs && own_buf && peer_flags && own_flags && out && (src_bits == 32 || src_bits == 64) &&
+                  count >= 1 && stride >= count && (op == 0 || op == 1) && n >= 1 && n <= ECO_MAX_PEERS &&
+                  rank >= 0 && rank < n && slot >= 0 && epoch > 0,
+              ECO_ERR_ARG, "eco_peer_allreduce_i64: bad arguments");
+  AllreduceArgs A{};
+  A.src = src;
+  A.src_bits = src_bits;
+  A.count = count;
+  A.stride = stride;
+  A.op = op;
+  A.n = n;
+  A.rank = rank;
+  A.slot = slot;
+  A.epoch = epoch;
+  for (int p = 0; p < n; ++p) {
+    ECO_REQUIRE(bufs[p] && peer_flags[p], ECO_ERR_ARG, "eco_peer_allreduce_i64: null buffer %d", p);
+    A.bufs[p] = bufs[p];
+    A.flags[p] = peer_flags[p];
+  }
+  A.own_buf = own_buf;
+  A.own_flags = own_flags;
+  A.out = out;
+  A.limit_ns = kPeerWaitNs;
+  peer_allreduce_kernel<<<1, 256, 0, eco_stream(stream)>>>(A);
+  return eco_launch_check("eco_peer_allreduce_i64");
 }

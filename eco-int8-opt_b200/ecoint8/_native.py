@@ -64,6 +64,10 @@ _SIGS = {
     "eco_requant_s32_s8_dev": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, SRSpec, c_p, c_i64, c_p, c_i64, c_p,
                                        c_p]),
     "eco_peer_push_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, c_i64, c_i64, c_i32, c_i32, c_p]),
+    "eco_peer_push_signal_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, c_i64, c_i64, c_i32, c_i32, c_p, c_i32,
+                                        c_i32, c_i32, c_i64, c_p, c_p]),
+    "eco_peer_allreduce_i64": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i64,
+                                       c_p, c_p]),
     "eco_peer_signal": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i64, c_p]),
     "eco_peer_wait": (c_i32, [c_p, c_i32, c_i32, c_i64, c_i64, c_p]),
     "eco_gemm_s8_requant": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_p, c_i32,

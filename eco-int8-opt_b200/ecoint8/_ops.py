@@ -114,11 +114,13 @@ def apply_mult_shift(x: torch.Tensor, mult, mult_kind: int, shift: int, site: Si
     return out
 
 
-def colsum(g: torch.Tensor) -> torch.Tensor:
+def colsum(g: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """int64 column sums of an int8 matrix (into ``out``, a contiguous int64 vector, if given)."""
     nat.require_cuda(g)
     g = _rowmajor(g)
     rows, cols = g.shape
-    out = torch.empty(cols, dtype=_I64, device=g.device)
+    if out is None:
+        out = torch.empty(cols, dtype=_I64, device=g.device)
     nat.call("eco_colsum_s8", g.data_ptr(), rows, cols, g.stride(0) if rows > 1 else cols, out.data_ptr(),
              nat.stream())
     return out

@@ -34,7 +34,9 @@ import torch.distributed as dist
 from . import _native as nat
 
 MAX_PEERS = 8  # ECO_MAX_PEERS of the C ABI
-MAX_SLOTS = 3 * 256  # three flag slots per row-sharded layer
+MAX_SLOTS = 3 * 256 + 1  # three flag slots per row-sharded layer, one for the small all-reduces
+RED_SLOT = MAX_SLOTS - 1
+RED_STRIDE = 1024  # longest vector of the small all-reduce
 
 
 def _arr(ptrs):
@@ -58,7 +60,7 @@ class Shared:
 class LayerBufs:
     def __init__(self, ex: "Exchange", layer, b: int):
         idx = len(ex.layers)
-        if 3 * idx + 3 > MAX_SLOTS:
+        if 3 * idx + 3 > RED_SLOT:
             raise RuntimeError("ecoint8.parallel: too many row-sharded layers for the peer exchange")
         self.slot_x, self.slot_dy, self.slot_w = 3 * idx, 3 * idx + 1, 3 * idx + 2
         n, dev, g = ex.n, ex.dev, ex.group
@@ -73,6 +75,7 @@ class LayerBufs:
         self.x_ptrs = _arr(self.x.ptrs)
         self.dy_ptrs = _arr(self.dy.ptrs)
         self.w_peers = _arr([p for r, p in enumerate(self.w.ptrs) if r != ex.rank])
+        self.done = torch.cuda.Event()  # the layer's dW rows are formed (recorded on the dW stream)
 
 
 class Exchange:
@@ -98,6 +101,10 @@ class Exchange:
         self.epoch = [0] * MAX_SLOTS
         self.comm = torch.cuda.Stream(device)
         self.dw = torch.cuda.Stream(device)
+        self._ev = torch.cuda.Event()  # reused: orders the communication stream after the current one
+        self.tickets = torch.zeros(MAX_SLOTS, dtype=torch.int32, device=device)  # push-and-signal tickets
+        self.red = Shared((2, self.n, RED_STRIDE), torch.int64, device, group)  # small all-reduce areas
+        self.red_ptrs = _arr(self.red.ptrs)
         self.layers: dict[int, LayerBufs] = {}
 
     # -- flags ------------------------------------------------------------------
@@ -109,8 +116,23 @@ class Exchange:
         if self.epoch[slot] > 0:
             nat.call("eco_peer_wait", self.flags.t.data_ptr(), self.n, slot, self.epoch[slot], 0, stream.cuda_stream)
 
+    def allreduce(self, src: torch.Tensor, op: str) -> torch.Tensor:
+        """MAX or SUM over the ranks of a short int32/int64 vector, as int64, on the current stream."""
+        n = src.numel()
+        if n > RED_STRIDE or src.dtype not in (torch.int32, torch.int64):
+            raise ValueError("the peer all-reduce takes at most 1024 int32/int64 values")
+        src = src.contiguous()
+        out = torch.empty(n, dtype=torch.int64, device=self.dev)
+        self.epoch[RED_SLOT] += 1
+        nat.call("eco_peer_allreduce_i64", src.data_ptr(), 32 if src.dtype == torch.int32 else 64, n,
+                 0 if op == "max" else 1, self.red_ptrs, RED_STRIDE, self.red.t.data_ptr(), self.flag_ptrs,
+                 self.flags.t.data_ptr(), self.n, self.rank, RED_SLOT, self.epoch[RED_SLOT], out.data_ptr(),
+                 nat.stream())
+        return out
+
     def _after_current(self, stream) -> None:
-        stream.wait_stream(torch.cuda.current_stream(self.dev))
+        self._ev.record(torch.cuda.current_stream(self.dev))
+        stream.wait_event(self._ev)
 
     # -- layers -----------------------------------------------------------------
     def layer(self, layer, b: int) -> LayerBufs:
@@ -121,31 +143,32 @@ class Exchange:
             raise RuntimeError(f"the peer exchange needs a fixed per-rank batch ({bufs.b}), got {b}")
         return bufs
 
+    def _push(self, src: int, ld: int, rows: int, cols: int, dst, n_dst: int, ld_dst: int, row0: int, split: int,
+              slot: int) -> None:
+        """One push kernel on the communication stream that signals ``slot`` when its stores are visible."""
+        self._after_current(self.comm)
+        self.epoch[slot] += 1
+        nat.call("eco_peer_push_signal_s8", src, ld, rows, cols, dst, n_dst, ld_dst, row0, split, self.ctas,
+                 self.flag_ptrs, self.n, self.rank, slot, self.epoch[slot], self.tickets[slot].data_ptr(),
+                 self.comm.cuda_stream)
+
     def push_input(self, bufs: LayerBufs, x: torch.Tensor) -> None:
         """This rank's input rows into every rank's ``x`` (rows rank * b ...)."""
-        self._after_current(self.comm)
-        nat.call("eco_peer_push_s8", x.data_ptr(), x.stride(0) if x.shape[0] > 1 else x.shape[1], x.shape[0],
-                 x.shape[1], bufs.x_ptrs, self.n, bufs.in_f, self.rank * bufs.b, 0, self.ctas,
-                 self.comm.cuda_stream)
-        self.signal(bufs.slot_x, self.comm)
+        self._push(x.data_ptr(), x.stride(0) if x.shape[0] > 1 else x.shape[1], x.shape[0], x.shape[1], bufs.x_ptrs,
+                   self.n, bufs.in_f, self.rank * bufs.b, 0, bufs.slot_x)
         x.record_stream(self.comm)
 
     def push_grad_columns(self, bufs: LayerBufs, g: torch.Tensor) -> None:
         """Column block p of this rank's dY rows into rank p's ``dy`` (rows rank * b ...)."""
-        self._after_current(self.comm)
-        nat.call("eco_peer_push_s8", g.data_ptr(), g.stride(0) if g.shape[0] > 1 else g.shape[1], g.shape[0],
-                 g.shape[1], bufs.dy_ptrs, self.n, bufs.out // self.n, self.rank * bufs.b, 1, self.ctas,
-                 self.comm.cuda_stream)
-        self.signal(bufs.slot_dy, self.comm)
+        self._push(g.data_ptr(), g.stride(0) if g.shape[0] > 1 else g.shape[1], g.shape[0], g.shape[1],
+                   bufs.dy_ptrs, self.n, bufs.out // self.n, self.rank * bufs.b, 1, bufs.slot_dy)
         g.record_stream(self.comm)
 
     def push_weight_rows(self, bufs: LayerBufs, lo: int, hi: int) -> None:
         """This rank's updated weight rows into the other ranks' ``w``."""
-        self._after_current(self.comm)
         w = bufs.w.t
-        nat.call("eco_peer_push_s8", w.data_ptr() + lo * bufs.in_f, bufs.in_f, hi - lo, bufs.in_f, bufs.w_peers,
-                 self.n - 1, bufs.in_f, lo, 0, self.ctas, self.comm.cuda_stream)
-        self.signal(bufs.slot_w, self.comm)
+        self._push(w.data_ptr() + lo * bufs.in_f, bufs.in_f, hi - lo, bufs.in_f, bufs.w_peers, self.n - 1,
+                   bufs.in_f, lo, 0, bufs.slot_w)
 
     def wait_weights(self, bufs: LayerBufs) -> None:
         self.wait(bufs.slot_w, torch.cuda.current_stream(self.dev))

@@ -253,11 +253,11 @@ def start_dw_rows_peer(layer, g_i8: torch.Tensor, s_g: float) -> None:
         ex.wait(bufs.slot_dy, dws)
         amax = torch.empty(1, dtype=torch.int32, device=bufs.x.t.device)
         red = _ops.gemm_s32(bufs.dy.t, 1, bufs.x.t, 1, hi - lo, bufs.in_f, bufs.x.t.shape[0], amax=amax)
-        gb_rows = _ops.colsum(bufs.dy.t)
-        done = torch.cuda.Event()
-        done.record(dws)
-    layer._dw_pending = {"red": red, "full": None, "shape": (bufs.out, bufs.in_f), "work": None, "gb": None,
-                         "gb_rows": gb_rows, "event": done, "rows": (lo, hi), "s_g": s_g, "amax": amax}
+        gb = torch.zeros(bufs.out, dtype=torch.int64, device=red.device)  # other rows: the flat SUM
+        _ops.colsum(bufs.dy.t, out=gb[lo:hi])
+        bufs.done.record(dws)
+    layer._dw_pending = {"red": red, "full": None, "shape": (bufs.out, bufs.in_f), "work": None, "gb": gb,
+                         "event": bufs.done, "rows": (lo, hi), "s_g": s_g, "amax": amax}
     _PENDING.append(layer)
 
 
@@ -279,10 +279,27 @@ def start_dw_rows(layer, dy_cols: torch.Tensor, a2a, s_g: float) -> None:
     _PENDING.append(layer)
 
 
+class _Done:
+    """The handle of an exchange that is already ordered on the current stream."""
+
+    def wait(self) -> None:
+        pass
+
+
 def start_max(amax: torch.Tensor):
     """Start the MAX over ranks of a device maximum; ``finish_max`` reads it."""
-    t = amax.reshape(1).to(torch.int64)
+    t = amax.reshape(1)
+    if _PEER is not None:  # one kernel through the peer exchange's buffers
+        return _PEER.allreduce(t, "max"), _Done()
     return t, dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_SMALL, async_op=True)
+
+
+def _small_reduce(t: torch.Tensor, op: str) -> torch.Tensor:
+    """MAX / SUM over ranks of a short vector (the peer exchange's kernel, else NCCL in place)."""
+    if _PEER is not None and t.numel() <= 1024:
+        return _PEER.allreduce(t, op).to(t.dtype)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM, group=_SMALL)
+    return t
 
 
 def finish_max(handle) -> int:
@@ -306,11 +323,8 @@ def finalize_pending() -> None:
         p = l._dw_pending
         if p.get("event") is not None:
             cur.wait_event(p["event"])
-            for t in (p["red"], p["amax"], p["gb_rows"]):
+            for t in (p["red"], p["amax"], p["gb"]):
                 t.record_stream(cur)
-            lo, hi = p["rows"]
-            p["gb"] = torch.zeros(p["shape"][0], dtype=torch.int64, device=p["red"].device)
-            p["gb"][lo:hi] = p["gb_rows"]  # the other rows arrive through the flat SUM below
     # the bias column sums of every pending layer in one all-reduce
     gbs = [l._dw_pending["gb"] for l in layers]
     flat = torch.cat(gbs)
@@ -330,7 +344,7 @@ def finalize_pending() -> None:
     else:
         maxima = torch.cat([a.to(torch.int64) if a is not None else _ops.amax(l._dw_pending["red"]).reshape(1)
                             for l, a in zip(layers, fused)])
-    dist.all_reduce(maxima, op=dist.ReduceOp.MAX, group=_SMALL)
+    maxima = _small_reduce(maxima, "max")
     sumsq = torch.zeros(len(layers), dtype=torch.int64, device=dev)
     queued = [bool(l._dw_pending.get("queued")) for l in layers]
     host = None if all(queued) else maxima.tolist()  # a queued backward keeps the maxima on the device
@@ -342,7 +356,7 @@ def finalize_pending() -> None:
             layer._finalize_dw(int(host[i]), sumsq[i:i + 1])
         if replicated and rank() != 0:  # every rank holds the whole layer: count it once
             sumsq[i:i + 1].zero_()
-    dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=_SMALL)
+    sumsq = _small_reduce(sumsq, "sum")
     for i, layer in enumerate(layers):
         layer._gw_sumsq = sumsq[i:i + 1]
         layer._gw_sumsq_of = layer.__dict__["_gw_i8_store"]
@@ -351,9 +365,8 @@ def finalize_pending() -> None:
 # -- optimizer --------------------------------------------------------------------
 def combine_step_state(state: torch.Tensor) -> None:
     """MAX of the row-max accumulators and error flags (columns 1, 2) over the row shards."""
-    part = state[:, 1:3].contiguous()
-    dist.all_reduce(part, op=dist.ReduceOp.MAX, group=_SMALL)
-    state[:, 1:3].copy_(part)
+    part = _small_reduce(state[:, 1:3].contiguous(), "max")
+    state[:, 1:3].copy_(part.view(-1, 2))
 
 
 def gather_rows(layer, rows) -> None:

@@ -195,6 +195,26 @@ ECO_API int eco_requant_s32_s8_dev(const int32_t* src, int64_t rows, int64_t col
 ECO_API int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst,
                      int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas, eco_stream_t stream);
 
+/* eco_peer_push_s8 that also publishes its completion: after every CTA's stores are
+ * fenced at system scope, the last CTA writes epoch into entry (slot, rank) of the
+ * n_ranks flag arrays (as eco_peer_signal; one launch instead of two).  ticket: a
+ * device word, zero before the call (the kernel leaves it zero), one per call in
+ * flight. */
+ECO_API int eco_peer_push_signal_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols,
+                            int8_t* const* dst, int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas,
+                            int64_t* const* peer_flags, int n_ranks, int rank, int slot, int64_t epoch,
+                            uint32_t* ticket, eco_stream_t stream);
+
+/* All-reduce (op 0: MAX, 1: SUM, int64 arithmetic) of count <= stride values (int32 or
+ * int64 at src) over the n ranks, result int64[count] in out.  bufs: the n ranks'
+ * exchange buffers, int64 [2][n][stride] each (own_buf: this rank's); flags as below,
+ * one slot used by every call in order, epoch growing by one per call.  Bounded wait
+ * (5 s; then out is zero and the error bit is set). */
+ECO_API int eco_peer_allreduce_i64(const void* src, int src_bits, int count, int op, int64_t* const* bufs,
+                           int stride, const int64_t* own_buf, int64_t* const* peer_flags,
+                           const int64_t* own_flags, int n, int rank, int slot, int64_t epoch, int64_t* out,
+                           eco_stream_t stream);
+
 /* Flag arrays are int64 [slots, ECO_MAX_PEERS], zero before first use.  signal:
  * after all prior work on the stream, writes epoch into entry (slot, rank) of
  * every rank's array (peer_flags: host array of the n ranks' flag pointers).

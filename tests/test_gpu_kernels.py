@@ -201,6 +201,17 @@ def test_peer_push_signal_and_bounded_wait_on_one_gpu():
     _native.call("eco_peer_wait", flags.data_ptr(), 1, 2, 7, 100000, s)
     torch.cuda.synchronize()
     assert int(flags[2, 0]) == 7 and _native.read_device_errors() == 0
+    # push and signal in one launch (every CTA fenced first); the ticket returns to zero
+    src = torch.randint(-127, 128, (300, 64), dtype=torch.int8, generator=gen).cuda()
+    dst = torch.zeros((300, 64), dtype=torch.int8, device="cuda")
+    ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
+    arr = (ctypes.c_void_p * 1)(dst.data_ptr())
+    _native.call("eco_peer_push_signal_s8", src.data_ptr(), 64, 300, 64, arr, 1, 64, 0, 0, 7, fl, 1, 0, 1, 3,
+                 ticket.data_ptr(), s)
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 1, 3, 100000, s)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src) and int(flags[1, 0]) == 3 and int(ticket) == 0
+    assert _native.read_device_errors() == 0
     _native.call("eco_peer_wait", flags.data_ptr(), 1, 3, 1, 100000, s)  # nothing signals slot 3
     torch.cuda.synchronize()
     assert _native.read_device_errors() == 4
