@@ -342,6 +342,7 @@ def main():
                     help="how ranks form the summed dW rows (ecoint8.parallel.init)")
     ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to the exchange under data parallelism")
     ap.add_argument("--push-ctas", type=int, default=16, help="CTAs per push kernel of the peer exchange")
+    ap.add_argument("--trace", default=None, help="with --profile: write rank 0's chrome trace to this file")
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")
     args = ap.parse_args()
@@ -484,7 +485,8 @@ def main():
             if rank == 0:
                 print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70),
                       file=sys.stderr)
-                prof.export_chrome_trace(str(REPO / "gpurun_out" / f"trace_n{world}.json"))
+                if args.trace:
+                    prof.export_chrome_trace(args.trace)
     if world > 1:
         import torch.distributed as dist
 

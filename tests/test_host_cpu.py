@@ -163,3 +163,26 @@ def test_replay_sites_follow_reference_order_without_gpu():
         s1 = _sr.draw((4, 5), 12, torch.device("cpu"), batch=True)
         s2 = _sr.draw((4, 5), -3, torch.device("cpu"), batch=True)  # left shift: no draw
     assert calls == [((4, 5), 4096)] and s1.nudge is not None and s2.nudge is None
+
+
+def test_device_scale_reads_and_overflow_flags_on_host_tensors():
+    """The device-scale holder turns the kernel's double bits into the reference's float, and
+    an overflow flag raised by the scale kernel becomes the reference's ValueError."""
+    import struct
+
+    from ecoint8 import _scale
+
+    bits = struct.unpack("<q", struct.pack("<d", 0.0123456789))[0]
+    s = _scale.DevScale(torch.tensor([bits, 1 << 30, 40], dtype=torch.int64))
+    assert float(s) == 0.0123456789 and _scale.as_float(s) == 0.0123456789 and _scale.as_float(2.5) == 2.5
+    assert _scale.gain_args(0.5) == (None, 0.5) and _scale.gain_args(s)[0] == s.t.data_ptr()
+    dev = torch.device("cpu")
+    f = _scale.flags(dev)
+    f.fill_(1)  # what the scale kernel sets for a shift beyond 62
+    with pytest.raises(ValueError, match="Overflow when unpacking long long"):
+        _scale.raise_flags(dev)
+    assert int(f) == 0
+    _scale.raise_flags(dev)  # cleared: no error
+    f.fill_(2)
+    with pytest.raises(AssertionError):
+        _scale.raise_flags(dev)
