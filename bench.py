@@ -338,10 +338,10 @@ def main():
     ap.add_argument("--only", choices=["gemm", "eco_step", "requant"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
-    ap.add_argument("--dw-exchange", default="gather", choices=["gather", "reduce", "peer"],
+    ap.add_argument("--dw-exchange", default="peer", choices=["gather", "reduce", "peer"],
                     help="how ranks form the summed dW rows (ecoint8.parallel.init)")
     ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to the exchange under data parallelism")
-    ap.add_argument("--push-ctas", type=int, default=16, help="CTAs per push kernel of the peer exchange")
+    ap.add_argument("--push-ctas", type=int, default=32, help="CTAs per push kernel of the peer exchange")
     ap.add_argument("--trace", default=None, help="with --profile: write rank 0's chrome trace to this file")
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")

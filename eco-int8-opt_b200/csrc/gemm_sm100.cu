@@ -18,7 +18,8 @@
 // Both operand majors are native: a K-major tile is a [rows][128 B] TMA box,
 // an MN-major tile is one or two [128 K rows][128 B] boxes, described to the
 // MMA by the canonical SWIZZLE_128B K-major / MN-major shared-memory layouts.
-// No TMA multicast (the kernels also run in multi-GPU jobs).
+// Every TMA load fills only the issuing CTA's own shared memory (the kernels also run in
+// multi-GPU jobs).
 // Every mbarrier wait is bounded by %globaltimer: on expiry the thread records
 // ECO_FLAG_WAIT_TIMEOUT in a device word and raises the CTA's abort flag, the
 // roles leave their loops, in-flight copies and MMAs are drained with bounded
