@@ -205,10 +205,11 @@ def time_kernel(fn, iters=10, warmup=3):
     return a.elapsed_time(b) / iters / 1e3  # s per launch
 
 
-def gemm_measurements(device):
+def gemm_measurements(device, M=16384, N=8192, K=8192):
+    """Fused forward GEMM (bias, per-column multipliers, Philox SR, ReLU), int32 GEMM, and
+    cuBLASLt's ``torch._int_mm`` (the reference's GEMM; None where it rejects the shape)."""
     from ecoint8 import _native, _ops, _sr
 
-    M, N, K = 16384, 8192, 8192
     gen = torch.Generator(device=device).manual_seed(1)
     x = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=device, generator=gen)
     w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=device, generator=gen)
@@ -218,10 +219,24 @@ def gemm_measurements(device):
     y = torch.empty((M, N), dtype=torch.int8, device=device)
     t_fused = time_kernel(lambda: _ops.gemm_requant(x, 0, w, 0, M, N, K, bias, mult, 36, True, site, out=y))
     t_s32 = time_kernel(lambda: _ops.gemm_s32(x, 0, w, 0, M, N, K))
-    t_cublas = time_kernel(lambda: torch._int_mm(x, w.t()))
+    try:
+        wt = w.t()
+        t_cublas = time_kernel(lambda: torch._int_mm(x, wt))
+    except RuntimeError:  # cuBLASLt's int8 GEMM needs K and N multiples of 8
+        t_cublas = None
     ops = 2.0 * M * N * K
     return {"shape": [M, N, K], "fused_requant_tops": ops / t_fused / 1e12, "fused_ms": t_fused * 1e3,
-            "s32_tops": ops / t_s32 / 1e12, "torch_int_mm_cublas_tops": ops / t_cublas / 1e12}, t_fused, ops
+            "s32_tops": ops / t_s32 / 1e12,
+            "torch_int_mm_cublas_tops": None if t_cublas is None else ops / t_cublas / 1e12}, t_fused, ops
+
+
+GEMM_SWEEP = [(1024, 1024, 1024), (4096, 4096, 4096), (4097, 4097, 4097), (8192, 8192, 8192),
+              (16384, 8192, 8192), (16384, 16384, 16384), (16384, 4097, 8192)]
+
+
+def gemm_sweep(device):
+    """Config 3: the GEMM at M, N, K from {1024, 4096, 8192, 16384} plus non-multiple-of-16 sizes."""
+    return [gemm_measurements(device, *mnk)[0] for mnk in GEMM_SWEEP]
 
 
 def requant_measurement(device, rows=16384, cols=8192):
@@ -335,7 +350,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
-    ap.add_argument("--only", choices=["gemm", "eco_step", "requant"],
+    ap.add_argument("--only", choices=["gemm", "gemm_sweep", "eco_step", "requant"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
     ap.add_argument("--dw-exchange", default="peer", choices=["gather", "reduce", "peer"],
@@ -351,6 +366,8 @@ def main():
         dev = torch.device("cuda", 0)
         if args.only == "gemm":
             res = gemm_measurements(dev)[0]
+        elif args.only == "gemm_sweep":
+            res = gemm_sweep(dev)
         elif args.only == "requant":
             res = requant_measurement(dev)
         else:
