@@ -186,3 +186,26 @@ def test_device_scale_reads_and_overflow_flags_on_host_tensors():
     f.fill_(2)
     with pytest.raises(AssertionError):
         _scale.raise_flags(dev)
+
+
+def test_reserved_philox_site_keeps_its_place_in_the_site_log():
+    """A key reserved for the dW site before the dX site is drawn stays first in the log,
+    even though the dW site is built (its shift known) after the dX site."""
+    from ecoint8 import _sr
+
+    torch.manual_seed(3)
+    _sr.LOG = []
+    try:
+        key_w = _sr.reserve_key()
+        site_x = _sr.draw((8, 4), 40, torch.device("cpu"), batch=True, kind="dx")
+        site_w = _sr.site_from_key(key_w, (4, 6), 37, 0, "dw")
+        key_n = _sr.reserve_key()
+        _sr.site_from_key(key_n, (2, 2), -1, 0, "dw")  # left shift: no draw, marked "none"
+        log = _sr.LOG
+    finally:
+        _sr.LOG = None
+    assert [e[0] for e in log] == ["dw", "dx", "none"]
+    assert log[0][1] == key_w and log[0][4] == 37 and log[1][4] == 40
+    assert site_w.spec.seed == key_w and site_x.spec.seed == log[1][1]
+    torch.manual_seed(3)  # the keys are the CPU generator's draws, in order
+    assert [_sr.new_key() for _ in range(3)] == [key_w, log[1][1], key_n]
