@@ -92,7 +92,11 @@ class Exchange:
         from torch.distributed import _symmetric_memory as symm
 
         if hasattr(symm, "enable_symm_mem_for_group") and not symm.is_symm_mem_enabled_for_group(group.group_name):
-            symm.enable_symm_mem_for_group(group.group_name)
+            import warnings
+
+            with warnings.catch_warnings():  # needed by older torch releases, a no-op that warns in newer ones
+                warnings.simplefilter("ignore", FutureWarning)
+                symm.enable_symm_mem_for_group(group.group_name)
         self.flags = Shared((MAX_SLOTS, MAX_PEERS), torch.int64, device, group)
         self.flags.t.zero_()
         torch.cuda.synchronize(device)
