@@ -226,6 +226,7 @@ ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 st
     for (int q = 0; q < 4; ++q) {
       const Philox4 rnd = sr_quad_k(keys, stream, row, (uint32_t)(4 * j + q));
       int wq[4], mq[4];
+      unsigned ties = 0u;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t f = quad_word(rnd, k);
@@ -241,14 +242,26 @@ ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 st
         rmn = min(rmn, m_new);
         rsum32 += abs(eU);
         const i64 p2 = mad_wide_u32(f >> 12, p2lo, mul_wide_s32(m_new, mmm));
-        int y;
-        if ((__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) & 0xFFFFFu) != 0xFFFFFu)
-          y = hi32(p2) >> shm;
-        else
-          y = (int)max((i64)-128, min((i64)128, step_m_round_tie(p2, c.com_mm, seed, stream, row,
-                                                                (uint32_t)(16 * j + 4 * q + k))));
+        // the tie-break draw matters only when bits [lo, lo + 20) of p2 are all ones
+        ties |= (unsigned)((__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) & 0xFFFFFu) == 0xFFFFFu) << k;
         wq[k] = wn;
-        mq[k] = max(min(y, 127), -127);
+        mq[k] = max(min(hi32(p2) >> shm, 127), -127);
+      }
+      if (ties) {  // rare (2^-20 per element): redo the tied elements with the exact draw
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!((ties >> k) & 1u)) continue;
+          const uint32_t f = quad_word(rnd, k);  // the element again, from its inputs
+          const int mU = shr_sel<HM>(mad_wide_s32(sbyte(mw[q], k), mmu, hm), cm);
+          const int gU = shr_sel<HG>(mad_wide_s32(sbyte(gw[q], k), mgu, hg), cg);
+          const int m_t = shr_fit(mad_wide_s32(gU, nbq, mul_wide_s32(mU, bq)), 16);
+          const int thU = sbyte(ww[q], k) * 4096 - shr_fit(mul_wide_s32(m_t, lrq), 16);
+          const int eU = thU - wq[k] * 4096;
+          const int m_new = m_t + shr_fit(mul_wide_s32(eU, aq), 16);
+          const i64 p2 = mad_wide_u32(f >> 12, p2lo, mul_wide_s32(m_new, mmm));
+          mq[k] = (int)max((i64)-127, min((i64)127, step_m_round_tie(p2, c.com_mm, seed, stream, row,
+                                                                    (uint32_t)(16 * j + 4 * q + k))));
+        }
       }
       wo[q] = pack4(wq[0], wq[1], wq[2], wq[3]);
       mo[q] = pack4(mq[0], mq[1], mq[2], mq[3]);

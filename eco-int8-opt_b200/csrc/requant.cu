@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
     for (int q = 0; q < 4; ++q) {
       const Philox4 rnd = sr_quad_k(a.keys, a.sr.stream, grow, (uint32_t)((c0 >> 2) + q));
       int y4[4];
+      unsigned ties = 0u;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int e = 4 * q + k;
@@ -224,11 +225,9 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
         int y;
         if (BIG) {
           const i64 p2 = mad_wide_u32(f, pow2lo, prod);  // prod + (f << lo)
-          if (__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) != 0xFFFFFFFFu)
-            y = hi32(p2) >> lo;  // (p2 >> shift) fits int32
-          else
-            y = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, f, a.sr.seed, a.sr.stream, grow,
-                                                           (uint32_t)c)));
+          // the tie-break draw matters only when bits [lo, lo + 32) of p2 are all ones
+          ties |= (unsigned)(__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) == 0xFFFFFFFFu) << k;
+          y = hi32(p2) >> lo;  // (p2 >> shift) fits int32
         } else if (sh >= 0 && !zero_out) {
           const u64 u = sh == 32 ? (u64)f : (u64)(f & ((1u << sh) - 1u));
           const i64 t = sar64(prod + (i64)u, sh);
@@ -239,8 +238,24 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
         } else {
           y = 0;
         }
-        y = max(min(y, 127), lower);  // saturate, ReLU
-        if (MASK && SUMSQ && mb[e] <= 0) y = 0;
+        y4[k] = y;
+      }
+      if (BIG && ties) {  // rare (2^-32 per element): redo the tied elements with the exact draw
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (!((ties >> k) & 1u)) continue;
+          const int c = c0 + 4 * q + k;
+          int x = v[4 * q + k];
+          if (BIAS) x = add32(x, a.bias[c]);
+          const i64 prod = mul_wide_s32(x, COLM ? a.mult_col[c] : mult_s);
+          y4[k] = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, quad_word(rnd, k), a.sr.seed, a.sr.stream,
+                                                             grow, (uint32_t)c)));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        int y = max(min(y4[k], 127), lower);  // saturate, ReLU
+        if (MASK && SUMSQ && mb[4 * q + k] <= 0) y = 0;
         if (SUMSQ) sq32 += y * y;
         y4[k] = y;
       }
