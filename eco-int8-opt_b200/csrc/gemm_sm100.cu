@@ -192,6 +192,42 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
   uint32_t packed[8];
   const uint32_t row = (uint32_t)(p.sr.row_base + m);
   const bool philox = p.sr.mode == ECO_SR_PHILOX && p.shift >= 0;
+  if (philox && p.shift > 32 && p.shift <= 62) {
+    // The usual forward case: single-instruction wide products, the 32-bit Philox field
+    // added in place by a multiply-add, the 2^-32 tie test out of the per-element branch
+    // (the warp redoes its tied elements together, so the shuffles stay convergent).
+    const int sh = p.shift, lo = sh - 32;
+    const uint32_t pow2lo = 1u << lo;
+    const int lower = p.relu ? 0 : -127;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const Philox4 rnd = sr_quad_k(p.keys, p.sr.stream, row, (uint32_t)((nb >> 2) + q));
+      int y4[4];
+      unsigned ties = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = 4 * q + k;
+        const int x = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
+        const i64 p2 = mad_wide_u32(quad_word(rnd, k), pow2lo,
+                                    mul_wide_s32(x, __shfl_sync(0xffffffffu, mult_lane, e)));
+        ties |= (unsigned)(__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) == 0xFFFFFFFFu) << k;
+        y4[k] = hi32(p2) >> lo;
+      }
+      if (__any_sync(0xffffffffu, ties != 0u)) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int e = 4 * q + k;
+          const int x = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
+          const i64 prod = mul_wide_s32(x, __shfl_sync(0xffffffffu, mult_lane, e));
+          if ((ties >> k) & 1u)
+            y4[k] = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, quad_word(rnd, k), p.sr.seed,
+                                                               p.sr.stream, row, (uint32_t)(nb + e))));
+        }
+      }
+      packed[q] = pack4(max(min(y4[0], 127), lower), max(min(y4[1], 127), lower), max(min(y4[2], 127), lower),
+                        max(min(y4[3], 127), lower));
+    }
+  } else {
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     Philox4 rnd{0u, 0u, 0u, 0u};
@@ -222,6 +258,7 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
       if (p.relu && y < 0) y = 0;
       packed[q] |= (uint32_t)(uint8_t)y << (8 * k);
     }
+  }
   }
   if (m >= p.M) return;
   int8_t* dst = p.Y + (i64)m * p.ldy + nb;
