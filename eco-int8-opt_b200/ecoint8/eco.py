@@ -17,7 +17,6 @@ import random
 
 import torch
 
-from . import _native
 from .quant import EPS  # noqa: F401  (re-exported like the reference)
 
 __all__ = ["EcoSGDM", "EcoAdam", "EcoInt8SGDM"]

@@ -29,7 +29,6 @@ from .fixedpoint import (
     quantize_multiplier,
     sar64,
     shl64,
-    sr_nudge_dtype,
     sub64,
     to_int8_sat,
 )
