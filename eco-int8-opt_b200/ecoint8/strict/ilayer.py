@@ -166,6 +166,24 @@ class I8Linear(nn.Module):
         else:
             super().__setattr__(name, value)
 
+    def __getstate__(self):
+        """Module state for ``torch.save(model)`` (the reference's way to persist): the
+        launch caches and in-flight exchange handles are dropped (rebuilt on use); device
+        scales of a queued backward are stored as their float values."""
+        d = nn.Module.__getstate__(self) if hasattr(nn.Module, "__getstate__") else dict(self.__dict__)
+        d = dict(d)
+        for k in ("_fwd_cache", "_sw_cache", "_input_gather", "_gather_works", "_sw_mean_cache"):
+            d.pop(k, None)
+        if d.get("_dw_pending") is not None:
+            raise RuntimeError("a data-parallel dW reduction is in flight: read a gradient or call "
+                               "ecoint8.parallel.synchronize() before saving")
+        for k in ("_gw_s_store", "_gb_s_store"):
+            if isinstance(d.get(k), _scale.DevScale):
+                d[k] = d[k].value()
+        d["_fwd_cache"] = None
+        d["_sw_cache"] = None
+        return d
+
     # Gradient stashes of the reference (ilayer.py:155-156, 168-169).  Under data
     # parallelism the dW reduction is still in flight when backward_i8 returns;
     # reading any of them completes every pending layer at once.

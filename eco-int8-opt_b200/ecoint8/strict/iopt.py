@@ -103,6 +103,24 @@ class I8ECO:
         self.step_count = 0
         self._stats = {"skipped": 0, "mean_abs_e": 0.0}
 
+    # -- checkpointing (torch.save of the optimizer, as of the reference's plain object) --
+    def __getstate__(self):
+        """The reference's state (layers, hyper-parameters, ``m_i8``, ``s_m``, ``stats``,
+        ``step_count``); device bookkeeping and launch caches are rebuilt after loading.
+        Under data parallelism, call ``parallel.synchronize`` and ``gather_momentum`` first."""
+        d = dict(self.__dict__)
+        if self._state is not None:
+            d["_s_m_host"] = [float(v) for v in self.s_m]  # reads the device (raises pending errors)
+            d["_stats"] = dict(self.stats)
+        for k in ("_plan_cache", "_keep_plan", "_flag_bufs", "_flag_turn", "_err", "_keep", "_rowsum_work"):
+            d.pop(k, None)
+        d.update(_state=None, _counter=None, _pending_stats=None, _err=None,
+                 _rowsum=[None] * len(self.layers))
+        return d
+
+    def __setstate__(self, d):
+        self.__dict__.update(d)
+
     # -- reference attributes ----------------------------------------------
     @property
     def s_m(self) -> list[float]:

@@ -386,3 +386,48 @@ def test_queued_backward_equals_layer_by_layer():
         return trail
 
     assert run(False) == run(True)
+
+
+def test_checkpoint_resume_equals_uninterrupted_training():
+    """torch.save((net, opt)) after two steps, load, two more steps: identical to four
+    uninterrupted steps (weights, momentum, biases, s_m)."""
+    import io
+
+    from ecoint8 import I8ECO, I8Linear, I8ReLU, I8Sequential
+
+    gen = torch.Generator().manual_seed(21)
+    X = torch.randn(64, 32, generator=gen)
+    yl = torch.randint(0, 4, (64,), generator=gen)
+
+    def setup():
+        torch.manual_seed(8)
+        net = I8Sequential(I8Linear(32, 64), I8ReLU(), I8Linear(64, 4)).cuda()
+        x0, sx0 = bnd.quantize_tensor_dynamic(X)
+        net.calibrate(x0.cuda(), sx0)
+        return net, I8ECO(net.int8_layers(), lr=0.3, momentum=0.9), net.quantize_input(X.cuda())[0]
+
+    def train(net, opt, x_i8, steps):
+        for _ in range(steps):
+            logits, s_out = net.forward_i8(x_i8)
+            _, g_fp = bnd.ce_grad(logits.cpu(), s_out, yl)
+            g_i8, s_g = bnd.quantize_tensor_dynamic(g_fp, stochastic=True)
+            net.backward_i8(g_i8.cuda(), s_g)
+            opt.step()
+            opt.zero_grad()
+
+    net, opt, x_i8 = setup()
+    train(net, opt, x_i8, 2)
+    buf = io.BytesIO()
+    torch.save((net, opt), buf)
+    rng = torch.get_rng_state()
+    train(net, opt, x_i8, 2)
+    want = [l.w_i8.cpu() for l in net.int8_layers()] + [m.cpu() for m in opt.m_i8] + [
+        l.b_acc.cpu() for l in net.int8_layers()]
+    want_sm = list(opt.s_m)
+    buf.seek(0)
+    net2, opt2 = torch.load(buf, weights_only=False)
+    torch.set_rng_state(rng)  # the Philox keys continue from the same CPU generator state
+    train(net2, opt2, x_i8, 2)
+    got = [l.w_i8.cpu() for l in net2.int8_layers()] + [m.cpu() for m in opt2.m_i8] + [
+        l.b_acc.cpu() for l in net2.int8_layers()]
+    assert all(torch.equal(a, b) for a, b in zip(want, got)) and list(opt2.s_m) == want_sm

@@ -209,3 +209,25 @@ def test_reserved_philox_site_keeps_its_place_in_the_site_log():
     assert site_w.spec.seed == key_w and site_x.spec.seed == log[1][1]
     torch.manual_seed(3)  # the keys are the CPU generator's draws, in order
     assert [_sr.new_key() for _ in range(3)] == [key_w, log[1][1], key_n]
+
+
+def test_optimizer_and_layers_pickle_like_the_reference():
+    """torch.save of the optimizer and of the layers (the reference's plain objects pickle);
+    launch caches are rebuilt after loading."""
+    import io
+
+    from ecoint8 import I8ECO, I8Linear
+
+    layers = [I8Linear(16, 8), I8Linear(8, 4, bias=False)]
+    opt = I8ECO(layers, lr=0.25, momentum=0.8, grad_clip=None)
+    opt.s_m = [0.5, 0.25]
+    opt.step_count = 3
+    opt._plan_cache = object()  # a launch cache that must not be pickled
+    buf = io.BytesIO()
+    torch.save((layers, opt), buf)
+    buf.seek(0)
+    layers2, opt2 = torch.load(buf, weights_only=False)
+    assert opt2.s_m == [0.5, 0.25] and opt2.step_count == 3 and opt2.lr == 0.25 and opt2.beta == 0.8
+    assert not hasattr(opt2, "_plan_cache") and opt2._state is None
+    assert all(torch.equal(a.w_i8, b.w_i8) for a, b in zip(layers, layers2))
+    assert all(torch.equal(a, b) for a, b in zip(opt.m_i8, opt2.m_i8))
