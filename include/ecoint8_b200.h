@@ -161,6 +161,8 @@ ECO_API int eco_split_cols_s8(const int8_t* src, int64_t ld_src, int64_t rows, i
  * backward pass is queued at once): the reference's dynamic_scale_from_int and
  * quantize_multiplier (fixedpoint.py:105-114, :26-37) in the same IEEE double
  * arithmetic, then the requant reads the multiplier and shift from the device.
+ * Replaces the host scale lines of I8Linear.backward_i8 (ilayer.py:153-154 for dW,
+ * :161-162 for dX) and the requants that follow them (:155, :163).
  *
  * eco_scale_from_amax: gain = (gain0_dev ? *gain0_dev (double bits) : gain0) * gain1;
  * s = amax * gain / 127 (1.0 when <= 0); (mult, shift) = quantize_multiplier(gain / s).
