@@ -50,7 +50,10 @@ def _peaks():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) while the timed region runs."""
+    """nvidia-smi samples (every 50 ms) while the timed region runs.  Entering waits (at
+    most 3 s) for the first sample, so that sampling is under way when the region opens;
+    only samples that arrive inside the region count, and when the region is shorter than
+    one period the sample taken just before it stands in (``samples`` says which)."""
 
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -64,12 +67,16 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.perf_counter()
+            while not self.lines and time.perf_counter() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
+        self.first = len(self.lines)  # samples before the timed region
         return self
 
     def _read(self):
@@ -87,7 +94,9 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        inside = self.lines[self.first:]
+        lines = inside if inside else self.lines[-1:]
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 8:
                 continue
@@ -102,13 +111,23 @@ class ClockSampler:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm) if inside else 0,
+                "sampled": "inside the timed region" if inside else "just before the (short) timed region"}
 
 
 # ----------------------------------------------------------------------------- launch counter
+def _step_kernels(layers, n, *rest) -> int:
+    """The I8ECO step kernel, plus the bias kernel when a row shard steps every bias."""
+    return 1 + int(any(layers[i].b_acc and layers[i].bias_rows > 0 for i in range(n)))
+
+
+# library kernels launched per C-ABI call (an int, or a function of the call's arguments)
 KERNELS_PER_CALL = {"eco_gemm_s8s32": 1, "eco_gemm_s8_requant": 1, "eco_requant_s32_s8": 1,
-                    "eco_apply_mult_shift": 1, "eco_colsum_s8": 1, "eco_amax": 2, "eco_sumsq_s8": 1,
-                    "eco_i8eco_step": 1, "eco_sgdm_step": 3}
+                    "eco_requant_s32_s8_dev": 2, "eco_scale_from_amax": 1, "eco_apply_mult_shift": 1,
+                    "eco_colsum_s8": 1, "eco_amax": 2, "eco_sumsq_s8": 1, "eco_split_cols_s8": 1,
+                    "eco_i8eco_step": _step_kernels, "eco_i8eco_finalize": 1, "eco_sgdm_step": 3,
+                    "eco_peer_push_s8": 1, "eco_peer_push_signal_s8": 1, "eco_peer_signal": 1,
+                    "eco_peer_wait": 1, "eco_peer_allreduce_i64": 1}
 
 
 class LaunchCounter:
@@ -121,7 +140,8 @@ class LaunchCounter:
 
     def __enter__(self):
         def counting(name, *args):
-            self.count += KERNELS_PER_CALL.get(name, 0)
+            k = KERNELS_PER_CALL.get(name, 0)
+            self.count += k(*args) if callable(k) else k
             return self.orig(name, *args)
 
         self.nat.call = counting
