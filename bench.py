@@ -6,38 +6,44 @@
 Headline (``value``): training steps/s of the deep strict-int8 MLP -- 8
 ``I8Linear(8192, 8192)`` + ``I8ReLU`` blocks and ``I8Linear(8192, 1000)`` --
 at a global batch of 16384 Gaussian samples with random labels, I8ECO
-(momentum 0.9).  One step = forward_i8 + the fp32 loss boundary (cross
-entropy, stochastic gradient quantization) + backward_i8 + I8ECO.step.  With N
-GPUs the global batch is split across ranks (strong scaling; int32 dW summed
-over NCCL).  Inputs are larger than L2 (no flush needed).
+(momentum 0.9).  One step = forward_i8 + the loss boundary (cross entropy and
+stochastic gradient quantization, fused: ``ecoint8.quant.cross_entropy_grad_i8``)
++ backward_i8 + I8ECO.step, with no host synchronisation inside the step.  With
+N GPUs the global batch (drawn once from one seed) is split across ranks
+(strong scaling); every exchange is exact, so all N print the same
+``weights_digest`` after the run.  Inputs are larger than L2 (no flush needed).
 
-Also measured on rank 0 at N=1: the fused forward GEMM (TOPS, the roofline
-kernel), the int32 GEMM, and the standalone I8ECO step over 64 layers of
-4096x4096 (HBM GB/s); and the oracle port of the reference on the host cores
-(``cpu_baseline``).  ``--impl reference`` times only that CPU port.
+Also measured on rank 0 at N=1: the GEMMs in their training layouts (the int32
+dX / dW GEMM is the step's dominant kernel, the roofline line), an int8 tensor
+peak measured on this GPU, the standalone I8ECO step over 64 layers of
+4096x4096 (config 4, HBM GB/s), the EcoInt8SGDM step at the same size, the
+backward requants, and the reference's own strict step on the host cores
+(``cpu_baseline``).  ``--impl reference`` times only that reference step.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import pathlib
 import statistics
+import struct
 import subprocess
 import sys
 import threading
 import time
 
 REPO = pathlib.Path(__file__).resolve().parent
-sys.path.insert(0, str(REPO / "eco-int8-opt_b200"))
 sys.path.insert(0, str(REPO))
-
-import torch  # noqa: E402
 
 LAYERS = [(8192, 8192)] * 8 + [(8192, 1000)]
 GLOBAL_BATCH = 16384
 METRIC = "int8 train steps/s (deep MLP 8x8192^2+8192->1000, global batch 16384)"
+WORKLOAD = ("config 5: deep strict-int8 MLP 8x I8Linear(8192,8192)+I8ReLU, I8Linear(8192,1000); Gaussian inputs, "
+            "random labels; I8ECO lr 0.05 momentum 0.9 grad_clip 1.0")
+LAYER_EQUIV = sum(a * b for a, b in LAYERS) / (8192 * 8192)  # the step's work in 8192^2-layer units
 
 
 def _peaks():
@@ -127,7 +133,8 @@ KERNELS_PER_CALL = {"eco_gemm_s8s32": 1, "eco_gemm_s8_requant": 1, "eco_requant_
                     "eco_colsum_s8": 1, "eco_amax": 2, "eco_sumsq_s8": 1, "eco_split_cols_s8": 1,
                     "eco_i8eco_step": _step_kernels, "eco_i8eco_finalize": 1, "eco_sgdm_step": 3,
                     "eco_peer_push_s8": 1, "eco_peer_push_signal_s8": 1, "eco_peer_signal": 1,
-                    "eco_peer_wait": 1, "eco_peer_allreduce_i64": 1}
+                    "eco_peer_wait": 1, "eco_peer_allreduce_i64": 1, "eco_ce_grad_rowstats": 1,
+                    "eco_ce_grad_quantize": 1}
 
 
 class LaunchCounter:
@@ -152,9 +159,11 @@ class LaunchCounter:
         self.nat.call = self.orig
 
 
-# ----------------------------------------------------------------------------- model
+# ----------------------------------------------------------------------------- model and data
 def fast_layer(in_f, out_f, gen, device):
     """I8Linear with the reference's init formula (ilayer.py:96-101) evaluated on the GPU."""
+    import torch
+
     from ecoint8 import I8Linear
 
     lin = I8Linear(1, 1)
@@ -168,6 +177,8 @@ def fast_layer(in_f, out_f, gen, device):
 
 
 def build_mlp(device, seed=0):
+    import torch
+
     from ecoint8 import I8ReLU, I8Sequential
 
     gen = torch.Generator(device=device).manual_seed(seed)
@@ -179,40 +190,53 @@ def build_mlp(device, seed=0):
     return I8Sequential(*blocks).to(device)
 
 
-HOST_BLOCKED = [0.0]  # seconds the host spent waiting in the loss boundary's read
+def global_batch(device, rank, world):
+    """This rank's rows of the global batch, drawn once from one seed on every rank
+    (Gaussian inputs, labels uniform over 1000 classes), and the batch's entry scale."""
+    import torch
+
+    from ecoint8.quant import calc_scale
+
+    gen = torch.Generator(device=device).manual_seed(100)
+    x = torch.randn(GLOBAL_BATCH, LAYERS[0][0], generator=gen, device=device)
+    y = torch.randint(0, LAYERS[-1][1], (GLOBAL_BATCH,), generator=gen, device=device)
+    s_x = calc_scale(x.abs().max().item())  # quantize_tensor_dynamic's scale, over the global batch
+    b = GLOBAL_BATCH // world
+    return x[rank * b:(rank + 1) * b].clone(), y[rank * b:(rank + 1) * b].clone(), s_x
 
 
-def loss_boundary(logits_i8, s_out, y, global_batch, world):
-    """fp32 boundary of examples/i8_demo.py:56-61: CE over the global batch, SR quantization of the grad."""
-    import torch.distributed as dist
+def train_step(net, opt, x_i8, y):
+    from ecoint8.quant import cross_entropy_grad_i8
 
-    from ecoint8.quant import calc_scale, quantize_symmetric
-
-    logits = (logits_i8.to(torch.float32) * s_out).requires_grad_()
-    loss = torch.nn.functional.cross_entropy(logits, y, reduction="sum") / global_batch
-    (g,) = torch.autograd.grad(loss, logits)
-    amax = g.detach().abs().max()
-    if world > 1:
-        dist.all_reduce(amax, op=dist.ReduceOp.MAX)
-        dist.all_reduce(loss, op=dist.ReduceOp.SUM)
-    t0 = time.perf_counter()
-    a = amax.item()  # the step's one host synchronisation
-    HOST_BLOCKED[0] += time.perf_counter() - t0
-    s_g = calc_scale(a)
-    return loss.detach(), quantize_symmetric(g, s_g, stochastic=True), s_g
-
-
-def train_step(net, opt, x_i8, y, world):
     logits, s_out = net.forward_i8(x_i8)
-    loss, g_i8, s_g = loss_boundary(logits, s_out, y, GLOBAL_BATCH, world)
+    loss, g_i8, s_g = cross_entropy_grad_i8(logits, s_out, y, count=GLOBAL_BATCH)
     net.backward_i8(g_i8, s_g)
     opt.step()
     opt.zero_grad()
     return loss
 
 
+def weights_digest(net, opt, world) -> str:
+    """sha256 of every layer's weights, momentum and bias accumulator and the momentum
+    scales after the run (momentum rows gathered from their owners under data parallelism)."""
+    from ecoint8 import parallel
+
+    if world > 1:
+        parallel.synchronize(net.int8_layers())
+        parallel.gather_momentum(opt)
+    h = hashlib.sha256()
+    for layer, m in zip(net.int8_layers(), opt.m_i8):
+        for t in (layer.w_i8, m, layer.b_acc):
+            h.update(t.contiguous().cpu().numpy().tobytes())
+    h.update(struct.pack(f"<{len(opt.s_m)}d", *opt.s_m))
+    h.update(float(opt.stats["mean_abs_e"]).hex().encode())
+    return h.hexdigest()[:24]
+
+
 # ----------------------------------------------------------------------------- side measurements
 def time_kernel(fn, iters=10, warmup=3):
+    import torch
+
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -226,8 +250,15 @@ def time_kernel(fn, iters=10, warmup=3):
 
 
 def gemm_measurements(device, M=16384, N=8192, K=8192):
-    """Fused forward GEMM (bias, per-column multipliers, Philox SR, ReLU), int32 GEMM, and
-    cuBLASLt's ``torch._int_mm`` (the reference's GEMM; None where it rejects the shape)."""
+    """The GEMMs of an 8192-wide layer at batch 16384 in their training layouts:
+
+    * fused forward (bias, per-column multipliers, Philox SR, ReLU): A = x [M,K], B = w [N,K];
+    * int32 + max|C| dX: A = g [M,K] (K-major), B = w stored [K,N] (MN-major);
+    * int32 + max|C| dW: A = g stored [K=batch, M] and B = x stored [K=batch, N] (both MN-major);
+    * cuBLASLt ``torch._int_mm`` (the reference's GEMM) at the forward shape.
+    """
+    import torch
+
     from ecoint8 import _native, _ops, _sr
 
     gen = torch.Generator(device=device).manual_seed(1)
@@ -237,17 +268,57 @@ def gemm_measurements(device, M=16384, N=8192, K=8192):
     mult = torch.randint(1 << 20, 1 << 21, (N,), dtype=torch.int32, device=device, generator=gen)
     site = _sr.Site(_native.sr_spec(_native.SR_PHILOX, seed=7, stream_id=0), None)
     y = torch.empty((M, N), dtype=torch.int8, device=device)
+    c = torch.empty((M, N), dtype=torch.int32, device=device)
+    amax = torch.empty(1, dtype=torch.int32, device=device)
     t_fused = time_kernel(lambda: _ops.gemm_requant(x, 0, w, 0, M, N, K, bias, mult, 36, True, site, out=y))
-    t_s32 = time_kernel(lambda: _ops.gemm_s32(x, 0, w, 0, M, N, K))
+
+    def s32(a, al, b, bl, m, n, k, out):
+        _native.call("eco_gemm_s8s32", a.data_ptr(), a.stride(0), al, b.data_ptr(), b.stride(0), bl, m, n, k, None,
+                     out.data_ptr(), n, amax.data_ptr(), _native.stream())
+
+    t_fwd32 = time_kernel(lambda: s32(x, 0, w, 0, M, N, K, c))
+    wt = torch.randint(-127, 128, (K, N), dtype=torch.int8, device=device, generator=gen)  # w stored [out=K, in=N]
+    t_dx = time_kernel(lambda: s32(x, 0, wt, 1, M, N, K, c))
+    # dW [out=N, in=K] over the batch M: A = g stored [M, N] (MN-major), B = x stored [M, K] (MN-major)
+    g = torch.randint(-127, 128, (M, N), dtype=torch.int8, device=device, generator=gen)
+    cw = torch.empty((N, K), dtype=torch.int32, device=device)
+    t_dw = time_kernel(lambda: s32(g, 1, x, 1, N, K, M, cw))
     try:
-        wt = w.t()
-        t_cublas = time_kernel(lambda: torch._int_mm(x, wt))
+        t_cublas = time_kernel(lambda: torch._int_mm(x, w.t()))
     except RuntimeError:  # cuBLASLt's int8 GEMM needs K and N multiples of 8
         t_cublas = None
     ops = 2.0 * M * N * K
-    return {"shape": [M, N, K], "fused_requant_tops": ops / t_fused / 1e12, "fused_ms": t_fused * 1e3,
-            "s32_tops": ops / t_s32 / 1e12,
-            "torch_int_mm_cublas_tops": None if t_cublas is None else ops / t_cublas / 1e12}, t_fused, ops
+    res = {"shape": [M, N, K], "fused_requant_tops": ops / t_fused / 1e12, "fused_ms": t_fused * 1e3,
+           "s32_fwd_layout_tops": ops / t_fwd32 / 1e12,
+           "s32_dx_tops": ops / t_dx / 1e12, "s32_dx_ms": t_dx * 1e3,
+           "s32_dw_tops": ops / t_dw / 1e12, "s32_dw_ms": t_dw * 1e3,
+           "torch_int_mm_cublas_tops": None if t_cublas is None else ops / t_cublas / 1e12}
+    return res, {"fused": t_fused, "dx": t_dx, "dw": t_dw}, ops
+
+
+def int8_peak(device):
+    """A dense int8 tensor-core peak measured on this GPU: the best of cuBLASLt's
+    ``torch._int_mm`` and this library's int32 GEMM over square and training shapes."""
+    import torch
+
+    from ecoint8 import _native
+
+    best, where = 0.0, None
+    for (M, N, K) in [(8192, 8192, 8192), (16384, 8192, 8192), (16384, 16384, 16384)]:
+        gen = torch.Generator(device=device).manual_seed(2)
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=device, generator=gen)
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=device, generator=gen)
+        c = torch.empty((M, N), dtype=torch.int32, device=device)
+        ops = 2.0 * M * N * K
+        for name, fn in (("cuBLASLt torch._int_mm", lambda: torch._int_mm(a, b.t())),
+                         ("gemm_s8_kernel", lambda: _native.call("eco_gemm_s8s32", a.data_ptr(), K, 0, b.data_ptr(),
+                                                                  K, 0, M, N, K, None, c.data_ptr(), N, None,
+                                                                  _native.stream()))):
+            tops = ops / time_kernel(fn, iters=8) / 1e12
+            if tops > best:
+                best, where = tops, f"{name} {M}x{N}x{K}"
+        del a, b, c
+    return best, where
 
 
 GEMM_SWEEP = [(1024, 1024, 1024), (4096, 4096, 4096), (4097, 4097, 4097), (8192, 8192, 8192),
@@ -255,14 +326,36 @@ GEMM_SWEEP = [(1024, 1024, 1024), (4096, 4096, 4096), (4097, 4097, 4097), (8192,
 
 
 def gemm_sweep(device):
-    """Config 3: the GEMM at M, N, K from {1024, 4096, 8192, 16384} plus non-multiple-of-16 sizes."""
-    return [gemm_measurements(device, *mnk)[0] for mnk in GEMM_SWEEP]
+    """Config 3: the fused GEMM at M, N, K from {1024, 4096, 8192, 16384} plus non-multiple-of-16 sizes."""
+    import torch
+
+    from ecoint8 import _native, _ops, _sr
+
+    out = []
+    for (M, N, K) in GEMM_SWEEP:
+        gen = torch.Generator(device=device).manual_seed(1)
+        x = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=device, generator=gen)
+        w = torch.randint(-127, 128, (N, K), dtype=torch.int8, device=device, generator=gen)
+        mult = torch.randint(1 << 20, 1 << 21, (N,), dtype=torch.int32, device=device, generator=gen)
+        site = _sr.Site(_native.sr_spec(_native.SR_PHILOX, seed=7, stream_id=0), None)
+        ops = 2.0 * M * N * K
+        t_f = time_kernel(lambda: _ops.gemm_requant(x, 0, w, 0, M, N, K, None, mult, 36, True, site))
+        t_s = time_kernel(lambda: _ops.gemm_s32(x, 0, w, 0, M, N, K))
+        try:
+            t_c = time_kernel(lambda: torch._int_mm(x, w.t()))
+        except RuntimeError:
+            t_c = None
+        out.append({"shape": [M, N, K], "fused_requant_tops": ops / t_f / 1e12, "s32_tops": ops / t_s / 1e12,
+                    "torch_int_mm_cublas_tops": None if t_c is None else ops / t_c / 1e12})
+    return out
 
 
 def requant_measurement(device, rows=16384, cols=8192):
     """The two backward requants of one 8192-wide layer at batch 16384, as training runs
     them: dX (int32 -> int8, Philox SR, scalar multiplier, ReLU mask; 4 + 1 + 1 B per
     element) and dW (8192 x 8192, square sum for the gradient clip; 4 + 1 B)."""
+    import torch
+
     from ecoint8 import _native, _ops, _sr
 
     gen = torch.Generator(device=device).manual_seed(3)
@@ -280,7 +373,10 @@ def requant_measurement(device, rows=16384, cols=8192):
 
 
 def eco_step_measurement(device, layers=64, dim=4096, steps=5):
-    """Config 4: I8ECO.step over 64 x 4096^2 int8 parameters (w, m, g uniform in [-127, 127])."""
+    """Config 4: I8ECO.step over 64 x 4096^2 int8 parameters (w, m, g uniform in [-127, 127]),
+    lr 0.05, momentum 0.9, grad_clip 1.0 (the default), ECO error injection on."""
+    import torch
+
     from ecoint8 import I8ECO, _ops
 
     gen = torch.Generator(device=device).manual_seed(2)
@@ -299,24 +395,110 @@ def eco_step_measurement(device, layers=64, dim=4096, steps=5):
         lin._gb_sum = torch.randint(-10 ** 6, 10 ** 6, (dim,), dtype=torch.int64, device=device, generator=gen)
         lin._gb_s = 1e-4
         lys.append(lin)
-    opt = I8ECO(lys, lr=0.05, momentum=0.9)
+    opt = I8ECO(lys, lr=0.05, momentum=0.9, grad_clip=1.0)
     for m in opt.m_i8:
         m.copy_(torch.randint(-127, 128, m.shape, dtype=torch.int8, device=device, generator=gen))
     opt.s_m = [3e-4] * layers
     t = time_kernel(opt.step, iters=steps, warmup=3)
     params = layers * dim * dim
-    return {"params": params, "bytes_per_param": 5, "ms": t * 1e3, "gbs": 5.0 * params / t / 1e9}
+    return {"params": params, "bytes_per_param": 5, "ms": t * 1e3, "gbs": 5.0 * params / t / 1e9,
+            "lr": 0.05, "momentum": 0.9, "grad_clip": 1.0}
+
+
+def sgdm_measurement(device, layers=64, dim=4096, steps=3):
+    """EcoInt8SGDM's fused step (the replacement of the reference's Triton kernels) over
+    64 x 4096^2 parameters: int8 w, m, fp32 g.  Algorithmic bytes 8 per parameter (read
+    w, m, g; write w, m); the step reads g and w, m again in its second pass because the
+    momentum scale is the maximum over the whole layer."""
+    import torch
+
+    from ecoint8 import EcoInt8SGDM, Int8Linear
+
+    gen = torch.Generator(device=device).manual_seed(4)
+    lys = []
+    for _ in range(layers):
+        lin = Int8Linear(1, 1, bias=False).to(device)
+        lin.w_i8 = torch.randint(-127, 128, (dim, dim), dtype=torch.int8, device=device, generator=gen)
+        lin.s_w = torch.rand((dim, 1), device=device, generator=gen) * 1e-2 + 1e-3
+        lin._grad_w = torch.randn((dim, dim), device=device, generator=gen) * 1e-3
+        lys.append(lin)
+    opt = EcoInt8SGDM(lys, lr=0.05, momentum=0.9)
+    grads = [l._grad_w for l in lys]
+
+    def step():  # the fused kernels alone, as EcoInt8SGDM.step calls them per layer
+        for i, (l, g) in enumerate(zip(lys, grads)):
+            opt._step_fused(i, l, g)
+
+    t = time_kernel(step, iters=steps, warmup=2)
+    params = layers * dim * dim
+    return {"params": params, "ms": t * 1e3, "bytes_per_param": 8, "gbs": 8.0 * params / t / 1e9,
+            "kernel_bytes_per_param": 18}
+
+
+# ----------------------------------------------------------------------------- the reference on the host
+def reference_layer_steps(max_samples: int, budget_s: float, batch: int = GLOBAL_BATCH):
+    """The reference's own strict step (compiled from its sources into oracle/_ref) on the
+    host cores: one I8Linear(8192, 8192) + I8ReLU at batch 16384 -- forward_i8,
+    I8ReLU.backward_mask, backward_i8, I8ECO.step -- per sample, on all host threads.
+    One untimed layer step first; then samples until ``max_samples`` or ``budget_s``.
+    Returns (seconds per layer step of each timed sample, info) or None when the
+    compiled reference is absent."""
+    from oracle import build_ref
+
+    ref = build_ref.load()
+    if ref is None:
+        return None
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)  # explicit: torchrun's OMP_NUM_THREADS=1 must not apply
+    strict, quant = ref["strict"], ref["quant"]
+    torch.manual_seed(0)
+    lin, relu = strict.I8Linear(8192, 8192), strict.I8ReLU()
+    x = torch.randn(batch, 8192)
+    x0, sx0 = quant.quantize_tensor_dynamic(x)
+    del x
+    lin.calibrate_forward(x0, sx0)
+    opt = strict.I8ECO([lin], lr=0.05, momentum=0.9)
+    g = torch.randint(-127, 128, (batch, 8192), dtype=torch.int8)
+
+    def layer_step():
+        y, _ = lin.forward_i8(x0)
+        relu.apply_forward(y)
+        lin.backward_i8(relu.backward_mask(g), 1e-4)
+        opt.step()
+        opt.zero_grad()
+
+    layer_step()  # untimed: first-touch allocations
+    times, t_all = [], time.perf_counter()
+    while len(times) < max(1, max_samples) and (not times or time.perf_counter() - t_all < budget_s):
+        t0 = time.perf_counter()
+        layer_step()
+        times.append(time.perf_counter() - t0)
+    info = {"threads": threads, "version": ref["version"], "torch": torch.__version__}
+    return times, info
+
+
+def cpu_baseline_subprocess():
+    """``cpu_baseline`` of the GPU arm: the reference arm (one untimed and one timed layer
+    step of the compiled reference) in a child process, so that the reference's own
+    ``ecoint8`` package never shares a process with this build's."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "OMP_NUM_THREADS")}
+    r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "0"], capture_output=True, text=True, env=env, timeout=1200)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"value": None, "unit": "steps/s", "cores": None, "kind": "unavailable",
+                "sample": f"reference arm failed (rc {r.returncode}): {r.stderr.strip()[-300:]}"}
+    return json.loads(lines[-1])["cpu_baseline"]
 
 
 def cpu_baseline_port():
-    """The oracle port of the reference strict step on the host cores, on a bounded sample.
-
-    Each part of one 8192->8192 layer is timed on a sample and scaled by its own
-    work to the full config-5 step (9 layers, batch 16384):
-    forward and dX (GEMM + requant) at batch 256 -> x 64; the dW GEMM on 256 output
-    rows at batch 256 -> x 32 x 64; the dW requant and the I8ECO step on 256 rows -> x 32.
-    """
+    """The oracle port of the reference strict step on the host cores (used only when the
+    compiled reference is absent), on a bounded sample scaled by work to the full step."""
     import numpy as np
+
+    import torch
 
     from oracle import fixedpoint as ofp
     from oracle import strict as ost
@@ -328,21 +510,21 @@ def cpu_baseline_port():
     w = rng.integers(-127, 128, (d, d), dtype=np.int8)
     x = rng.integers(-127, 128, (b, d), dtype=np.int8)
     g = rng.integers(-127, 128, (b, d), dtype=np.int8)
-    wf = w.astype(np.float64)  # the port's exact GEMM format (ofp.int_mm), converted once per step
+    wf = w.astype(np.float64)
     sw = [1e-2 + 1e-6 * i for i in range(d)]
     draw = ost.TorchDraws()
 
-    def mm(a, bf):  # ofp.int_mm with the right operand already in float64
+    def mm(a, bf):
         return (a.astype(np.float64) @ bf).astype(np.int64).astype(np.int32)
 
     t0 = time.perf_counter()
-    ost.common_shift_requant(mm(x, wf.T), [0.02 * s / 0.5 for s in sw], draw)  # forward
+    ost.common_shift_requant(mm(x, wf.T), [0.02 * s / 0.5 for s in sw], draw)
     dx = mm(g, wf)
     m, sh = ofp.quantize_multiplier(1e-4)
-    ofp.to_int8_sat(ofp.apply_mult_shift(dx, m, sh, True, draw(dx.shape, 1 << sh)))  # dX
+    ofp.to_int8_sat(ofp.apply_mult_shift(dx, m, sh, True, draw(dx.shape, 1 << sh)))
     t_batch = time.perf_counter() - t0
     t0 = time.perf_counter()
-    dw = ofp.int_mm(g[:, :rows].T, x)  # dW rows, K = batch sample
+    dw = ofp.int_mm(g[:, :rows].T, x)
     t_dw = time.perf_counter() - t0
     t0 = time.perf_counter()
     gw = ofp.to_int8_sat(ofp.apply_mult_shift(dw, m, sh, True, draw(dw.shape, 1 << sh)))
@@ -352,14 +534,43 @@ def cpu_baseline_port():
     sub._gb_sum, sub._gb_s = g[:, :rows].astype(np.int64).sum(0), 3e-5
     ost.I8ECO([sub], lr=0.05).step(draw)
     t_rows = time.perf_counter() - t0
-    layer_equiv = sum(a * o for a, o in LAYERS) / (d * d)
-    t_full = layer_equiv * (t_batch * GLOBAL_BATCH / b + t_dw * (d / rows) * (GLOBAL_BATCH / b)
-                            + t_rows * d / rows)
+    t_full = LAYER_EQUIV * (t_batch * GLOBAL_BATCH / b + t_dw * (d / rows) * (GLOBAL_BATCH / b) + t_rows * d / rows)
     return {"value": 1.0 / t_full, "unit": "steps/s", "cores": threads, "kind": "port",
             "sample": f"numpy oracle port of one 8192x8192 layer: fwd+dX at batch {b} ({t_batch:.2f} s), dW GEMM "
                       f"{rows} rows x batch {b} ({t_dw:.2f} s), dW requant + I8ECO step on {rows} rows "
-                      f"({t_rows:.2f} s); scaled by work to 9 layers x batch {GLOBAL_BATCH}",
-            "seconds_per_step_estimate": t_full}
+                      f"({t_rows:.2f} s); scaled by work to 9 layers x batch {GLOBAL_BATCH} (the compiled "
+                      f"reference was absent)"}
+
+
+def run_reference_arm(args, rank):
+    """``--impl reference``: the reference's own CPU strict step (rank 0 only)."""
+    if rank != 0:
+        return
+    t_wall = time.perf_counter()
+    r = reference_layer_steps(max_samples=args.steps, budget_s=60.0)
+    if r is not None:
+        times, info = r
+        t = statistics.median(times)
+        value = 1.0 / (t * LAYER_EQUIV)
+        timed_steps = len(times) / LAYER_EQUIV  # training steps' worth of layer steps actually timed
+        cb = {"value": value, "unit": "steps/s", "cores": info["threads"], "kind": "reference",
+              "sample": f"reference ecoint8 {info['version']} (torch {info['torch']} CPU, compiled into oracle/_ref) "
+                        f"strict step of one I8Linear(8192,8192)+I8ReLU at batch {GLOBAL_BATCH}: {len(times)} "
+                        f"layer steps timed (of --steps {args.steps}, within a 60 s budget; one untimed first), "
+                        f"median {t:.2f} s; x {LAYER_EQUIV:.3f} layer equivalents per training step"}
+        ms = 1e3 * t * LAYER_EQUIV
+        dtype = "int64"
+    else:
+        cb = cpu_baseline_port()
+        value, ms, timed_steps, dtype = cb["value"], 1e3 / cb["value"], None, "int64"
+    print(json.dumps({"impl": "reference", "metric": METRIC, "value": value, "unit": "steps/s",
+                      "n_gpus": args.gpus, "steps": timed_steps if timed_steps is not None else args.steps,
+                      "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                      "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+                      "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "parallelism": "host cores",
+                                 "wall_s": time.perf_counter() - t_wall},
+                      "cpu_baseline": cb,
+                      "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
 # ----------------------------------------------------------------------------- main
@@ -370,7 +581,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
-    ap.add_argument("--only", choices=["gemm", "gemm_sweep", "eco_step", "requant"],
+    ap.add_argument("--only", choices=["gemm", "gemm_sweep", "eco_step", "requant", "sgdm", "peak"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
     ap.add_argument("--dw-exchange", default="peer", choices=["gather", "reduce", "peer"],
@@ -381,47 +592,26 @@ def main():
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")
     args = ap.parse_args()
-    if args.only:
-        torch.cuda.set_device(0)
-        dev = torch.device("cuda", 0)
-        if args.only == "gemm":
-            res = gemm_measurements(dev)[0]
-        elif args.only == "gemm_sweep":
-            res = gemm_sweep(dev)
-        elif args.only == "requant":
-            res = requant_measurement(dev)
-        else:
-            res = eco_step_measurement(dev, layers=args.eco_layers)
-        print(json.dumps({args.only: res}))
-        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank)
+
+    sys.path.insert(0, str(REPO / "eco-int8-opt_b200"))
+    import torch
+
+    if args.only:
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        res = {"gemm": lambda: gemm_measurements(dev)[0], "gemm_sweep": lambda: gemm_sweep(dev),
+               "requant": lambda: requant_measurement(dev), "sgdm": lambda: sgdm_measurement(dev),
+               "peak": lambda: int8_peak(dev),
+               "eco_step": lambda: eco_step_measurement(dev, layers=args.eco_layers)}[args.only]()
+        print(json.dumps({args.only: res}))
+        return
     if args.gpus > 1 and world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} needs torchrun with {args.gpus} ranks (WORLD_SIZE={world})")
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        vals = []
-        for _ in range(args.warmup):
-            cpu_baseline_port()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            vals.append(cpu_baseline_port())
-        el = time.perf_counter() - t0
-        v = statistics.median(x["value"] for x in vals)
-        cb = dict(vals[-1])
-        cb["value"] = v
-        print(json.dumps({"impl": "reference", "metric": METRIC, "value": v, "unit": "steps/s",
-                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                          "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "strong",
-                          "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-                          "config": {"workload": "config 5 deep MLP", "global_batch": GLOBAL_BATCH,
-                                     "parallelism": f"dp{args.gpus}", "sampled_wall_s": el},
-                          "cpu_baseline": cb,
-                          "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
-        return
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -433,23 +623,20 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     from ecoint8 import I8ECO, parallel
     from ecoint8._sr import batch_rows, set_generator
+    from ecoint8.strict import iopt
 
     if world > 1:
         parallel.init(dw_exchange=args.dw_exchange, comm_sms=args.comm_sms, push_ctas=args.push_ctas)
     set_generator(torch.Generator().manual_seed(1234))  # identical Philox keys on every rank
     local_b = GLOBAL_BATCH // world
-    torch.manual_seed(0)
     net = build_mlp(device)
-    gen = torch.Generator(device=device).manual_seed(100 + rank)
-    x_fp = torch.randn(local_b, LAYERS[0][0], device=device, generator=gen)
-    y = torch.randint(0, LAYERS[-1][1], (local_b,), device=device, generator=gen)
-    from ecoint8.quant import quantize_tensor_dynamic
-
+    x_fp, y, sx0 = global_batch(device, rank, world)
     with batch_rows(rank * local_b):
-        x0, sx0 = quantize_tensor_dynamic(x_fp)
-        net.calibrate(x0, sx0)
+        from ecoint8.quant import quantize_symmetric
+
+        net.calibrate(quantize_symmetric(x_fp, sx0), sx0)
         x_i8 = net.quantize_input(x_fp)[0]
-        del x_fp, x0
+        del x_fp
         opt = I8ECO(net.int8_layers(), lr=0.05, momentum=0.9)
 
         def barrier():
@@ -457,7 +644,7 @@ def main():
                 torch.distributed.barrier()
 
         for _ in range(args.warmup):
-            train_step(net, opt, x_i8, y, world)
+            train_step(net, opt, x_i8, y)
         torch.cuda.synchronize()
         barrier()
         counter = LaunchCounter()
@@ -465,14 +652,14 @@ def main():
         with ClockSampler(local) as clk, counter:
             torch.cuda.synchronize()
             barrier()
-            HOST_BLOCKED[0] = 0.0
+            iopt.HOST_WAIT_S[0] = 0.0
             w0 = time.perf_counter()
             ev0.record()
             for _ in range(args.steps):
-                train_step(net, opt, x_i8, y, world)
+                train_step(net, opt, x_i8, y)
             ev1.record()
             host_wall = time.perf_counter() - w0
-            host_blocked = HOST_BLOCKED[0]
+            host_blocked = iopt.HOST_WAIT_S[0]
             torch.cuda.synchronize()
             barrier()
         ms = ev0.elapsed_time(ev1)
@@ -506,7 +693,9 @@ def main():
             yb.record_stream(cur)
             if i + 1 < args.steps:
                 nxt = fetch()
-            loss = train_step(net, opt, xb, yb, world)
+            loss = train_step(net, opt, xb, yb)
+            if world > 1:
+                torch.distributed.all_reduce(loss)  # the mean over the global batch
             float(loss.item())
         e1.record()
         torch.cuda.synchronize()
@@ -517,13 +706,14 @@ def main():
 
             with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
                 for _ in range(3):
-                    train_step(net, opt, x_i8, y, world)
+                    train_step(net, opt, x_i8, y)
                 torch.cuda.synchronize()
             if rank == 0:
                 print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70),
                       file=sys.stderr)
                 if args.trace:
                     prof.export_chrome_trace(args.trace)
+        digest = weights_digest(net, opt, world)
     if world > 1:
         import torch.distributed as dist
 
@@ -532,46 +722,55 @@ def main():
         ms, ms_e2e = t.tolist()
     value = args.steps / (ms / 1e3)
     e2e = args.steps / (ms_e2e / 1e3)
-    out = None
     if rank == 0:
         hbm, bf16, src = _peaks()
-        int8_peak = 2.0 * bf16  # dense int8 = 2x dense bf16 on B200 (no measured int8 peak)
         out = {"metric": METRIC, "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                "scaling": "strong", "vs_baseline": None, "dtype": "int8/int32/int64", "data": "synthetic",
-               "config": {"workload": "config 5: deep strict-int8 MLP 8x I8Linear(8192,8192)+I8ReLU, "
-                                      "I8Linear(8192,1000); Gaussian inputs, random labels; I8ECO momentum 0.9",
-                          "global_batch": GLOBAL_BATCH, "per_gpu_batch": local_b, "parallelism": f"dp{world}",
-                          "dw_exchange": args.dw_exchange if world > 1 else None,
+               "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "per_gpu_batch": local_b,
+                          "parallelism": f"dp{world}", "dw_exchange": args.dw_exchange if world > 1 else None,
                           "comm_sms": args.comm_sms if world > 1 else None,
                           "push_ctas": args.push_ctas if world > 1 and args.dw_exchange == "peer" else None,
-                          "l2": "inputs larger than L2 (1.2 GB activations + 0.55 GB weights); no flush"},
+                          "l2": "inputs larger than L2 (1.2 GB activations + 0.55 GB weights); no flush",
+                          "data": "global batch drawn once from seed 100, rows split across ranks"},
                "e2e": {"value": e2e, "unit": "steps/s", "h2d_bytes_per_step": int(x_i8.numel() + y.numel() * 8),
                        "d2h_bytes_per_step": 4},
                "gpu_launches": launches, "clocks": clk.summary(),
                "host": {"issue_ms_per_step": 1e3 * (host_wall - host_blocked) / args.steps,
-                        "blocked_ms_per_step": 1e3 * host_blocked / args.steps}}
+                        "blocked_ms_per_step": 1e3 * host_blocked / args.steps},
+               "weights_digest": digest}
         if world == 1 and not args.no_side:
-            gm, t_fused, ops = gemm_measurements(device)
+            gm, times, ops = gemm_measurements(device)
             out["gemm"] = gm
+            peak, peak_where = int8_peak(device)
+            gm["int8_peak_tops"], gm["int8_peak_source"] = peak, peak_where
             out["eco_step"] = eco_step_measurement(device)
-            out["requant"] = requant_measurement(device)
-            achieved = ops / t_fused / 1e12
-            out["roofline"] = {"bound": "tensor", "kernel": "gemm_s8_kernel<256,1> (fused forward, 16384x8192x8192)",
-                               "achieved": achieved, "peak": int8_peak, "unit": "TFLOP/s",
-                               "peak_source": f"2 x {src} bf16 dense ({bf16} TFLOP/s)",
-                               "frac": achieved / int8_peak, "traffic": _traffic()}
             out["eco_step"]["frac_of_hbm"] = out["eco_step"]["gbs"] / hbm
-            out["cpu_baseline"] = {k: v for k, v in cpu_baseline_port().items() if k != "seconds_per_step_estimate"}
+            out["sgdm_step"] = sgdm_measurement(device)
+            out["sgdm_step"]["frac_of_hbm"] = out["sgdm_step"]["gbs"] / hbm
+            out["requant"] = requant_measurement(device)
+            achieved = ops / times["dx"] / 1e12
+            out["roofline"] = {"bound": "tensor",
+                               "kernel": "gemm_s8_kernel<256,0> (int32 + max|C|, the dX GEMM: 16384x8192x8192, "
+                                         "B MN-major; 26 of the step's GEMM launches are this kernel)",
+                               "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                               "peak_source": f"measured int8 dense peak on this GPU: best of {peak_where} "
+                                              f"(2 x {src} bf16 = {2 * bf16:.0f} for context)",
+                               "frac": achieved / peak, "traffic": _traffic("gemm_s32_dx_16384x8192x8192.md"),
+                               "dw": {"achieved": ops / times["dw"] / 1e12, "frac": ops / times["dw"] / 1e12 / peak,
+                                      "shape": "8192x8192 over batch 16384, A and B MN-major"},
+                               "fused_forward": {"achieved": ops / times["fused"] / 1e12,
+                                                 "frac": ops / times["fused"] / 1e12 / peak}}
+            out["cpu_baseline"] = cpu_baseline_subprocess()
         print(json.dumps(out))
     if world > 1:
         parallel.shutdown()
         torch.distributed.destroy_process_group()
 
 
-def _traffic():
-    """DRAM bytes per launch of the roofline kernel, from the committed ncu summary (or None)."""
-    p = REPO / "profiles" / "gemm_fwd_fused_16384x8192x8192.md"
+def _traffic(name):
+    """DRAM bytes per launch of the roofline kernel, from its committed ncu summary (or None)."""
+    p = REPO / "profiles" / name
     if p.exists():
         for line in p.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):

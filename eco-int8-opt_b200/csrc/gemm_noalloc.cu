@@ -23,7 +23,10 @@
 //     overwrites what the last one left;
 //   * the first call on each device looks up the buffer's device address
 //     (cudaGetSymbolAddress) with that device current; make that first call
-//     before any stream capture.
+//     before any stream capture.  The address is cached for the lifetime of
+//     the device's primary context: a host that calls cudaDeviceReset (or
+//     otherwise tears the primary context down) must not call this entry
+//     point on that device again in the same process.
 #include <mutex>
 
 #include "abi.cuh"
@@ -63,7 +66,11 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 extern "C" int eco_gemm_s8s32_noalloc(const int8_t* A, int64_t lda, int a_layout, const int8_t* B, int64_t ldb,
                                       int b_layout, int64_t M, int64_t N, int64_t K, const int32_t* bias,
                                       int32_t* C, int64_t ldc, int32_t* amax, eco_stream_t stream) {
+  // every check of the GEMM itself comes first, so a call that will be rejected queues no relayout
   ECO_REQUIRE(A && B && C && M > 0 && N > 0 && K > 0, ECO_ERR_ARG, "eco_gemm_s8s32_noalloc: bad arguments");
+  ECO_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), ECO_ERR_ARG,
+              "eco_gemm_s8s32_noalloc: dims too large");
+  ECO_REQUIRE(ldc >= N, ECO_ERR_ARG, "eco_gemm_s8s32_noalloc: ldc < N");
   ECO_REQUIRE((a_layout == 0 || a_layout == 1) && (b_layout == 0 || b_layout == 1), ECO_ERR_ARG,
               "eco_gemm_s8s32_noalloc: layout");
   // stored shapes: A is [M, K] (layout 0) or [K, M]; B is [N, K] (layout 0) or [K, N]

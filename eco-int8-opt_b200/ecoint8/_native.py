@@ -17,7 +17,7 @@ _PKG_ROOT = pathlib.Path(__file__).resolve().parent.parent
 LIB_PATH = _PKG_ROOT / "lib" / "libecoint8_b200.so"
 
 ECO_OK = 0
-SR_NEAREST, SR_PHILOX, SR_REPLAY32, SR_REPLAY64 = 0, 1, 2, 3
+SR_NEAREST, SR_PHILOX, SR_REPLAY32, SR_REPLAY64, SR_REPLAY_F32 = 0, 1, 2, 3, 4
 FLAG_SHIFT_OVERFLOW, FLAG_BAD_RATIO, FLAG_WAIT_TIMEOUT = 1, 2, 4
 
 c_i64, c_u64, c_i32, c_u32, c_p, c_d, c_f = (ctypes.c_int64, ctypes.c_uint64, ctypes.c_int32, ctypes.c_uint32,
@@ -70,6 +70,12 @@ _SIGS = {
                                        c_p, c_p]),
     "eco_peer_signal": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i64, c_p]),
     "eco_peer_wait": (c_i32, [c_p, c_i32, c_i32, c_i64, c_i64, c_p]),
+    "eco_ce_grad_rowstats": (c_i32, [c_p, c_i64, c_i64, c_i64, c_d, c_p, c_i64, c_p, c_p, c_p, c_p]),
+    "eco_ce_grad_quantize": (c_i32, [c_p, c_i64, c_i64, c_i64, c_d, c_p, c_i64, c_p, c_p, c_i32, SRSpec, c_p, c_i64,
+                                     c_p, c_p, c_p, c_p, c_p]),
+    "eco_ipc_export": (c_i32, [c_p, c_p, ctypes.POINTER(c_i64)]),
+    "eco_ipc_open": (c_i32, [c_p, ctypes.POINTER(c_p)]),
+    "eco_ipc_close": (c_i32, [c_p]),
     "eco_gemm_s8_requant": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_p, c_i32,
                                     c_i32, SRSpec, c_p, c_i64, c_p]),
     "eco_requant_s32_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_p, c_i64, c_i32, c_i32, SRSpec, c_p, c_i64,

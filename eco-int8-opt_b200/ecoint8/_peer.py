@@ -1,5 +1,6 @@
 """The "peer" exchange of data parallelism: NVLink stores into buffers that every
-rank allocates and maps (torch symmetric memory), ordered by flag barriers.
+rank allocates and maps into the other ranks' processes (CUDA IPC handles: plain
+unicast peer mappings, never an NVLink multicast object), ordered by flag barriers.
 
 Per row-sharded layer every rank holds
 
@@ -37,24 +38,48 @@ MAX_PEERS = 8  # ECO_MAX_PEERS of the C ABI
 MAX_SLOTS = 3 * 256 + 1  # three flag slots per row-sharded layer, one for the small all-reduces
 RED_SLOT = MAX_SLOTS - 1
 RED_STRIDE = 1024  # longest vector of the small all-reduce
+HANDLE_BYTES = 64  # ECO_IPC_HANDLE_BYTES of the C ABI
 
 
 def _arr(ptrs):
     return (ctypes.c_void_p * len(ptrs))(*ptrs)
 
 
+class IpcMaps:
+    """The peer allocations this process has mapped (one mapping per allocation: several
+    exchange buffers can live in one allocation of the caching allocator)."""
+
+    def __init__(self):
+        self.opened: dict[tuple[int, bytes], int] = {}
+
+    def open(self, rank: int, handle: bytes) -> int:
+        base = self.opened.get((rank, handle))
+        if base is None:
+            p = ctypes.c_void_p()
+            nat.call("eco_ipc_open", handle, ctypes.byref(p))
+            base = self.opened[(rank, handle)] = int(p.value)
+        return base
+
+    def close_all(self) -> None:
+        for base in self.opened.values():
+            nat.call("eco_ipc_close", base)
+        self.opened.clear()
+
+
 class Shared:
-    """A tensor allocated on every rank of ``group`` with the device pointers of all copies.
-    Collective: every rank creates the same sequence of them."""
+    """A tensor allocated on every rank of ``group`` with the device pointers of all copies
+    (the other ranks' copies mapped through CUDA IPC).  Collective: every rank creates the
+    same sequence of them."""
 
-    def __init__(self, shape, dtype, device, group):
-        from torch.distributed import _symmetric_memory as symm
-
-        self.t = symm.empty(*shape, dtype=dtype, device=device)
-        self.handle = symm.rendezvous(self.t, group)
-        h = self.handle
-        off = self.t.data_ptr() - h.buffer_ptrs[h.rank]
-        self.ptrs = [int(b) + off for b in h.buffer_ptrs]
+    def __init__(self, shape, dtype, device, group, maps: IpcMaps):
+        self.t = torch.empty(shape, dtype=dtype, device=device)
+        handle = ctypes.create_string_buffer(HANDLE_BYTES)
+        off = ctypes.c_int64()
+        nat.call("eco_ipc_export", self.t.data_ptr(), handle, ctypes.byref(off))
+        n, me = dist.get_world_size(group), dist.get_rank(group)
+        every = [None] * n
+        dist.all_gather_object(every, (handle.raw, off.value), group=group)
+        self.ptrs = [self.t.data_ptr() if r == me else maps.open(r, h) + o for r, (h, o) in enumerate(every)]
 
 
 class LayerBufs:
@@ -66,9 +91,9 @@ class LayerBufs:
         n, dev, g = ex.n, ex.dev, ex.group
         out, in_f = layer.w_i8.shape
         self.b, self.out, self.in_f = b, out, in_f
-        self.x = Shared((n * b, in_f), torch.int8, dev, g)
-        self.dy = Shared((n * b, out // n), torch.int8, dev, g)
-        self.w = Shared((out, in_f), torch.int8, dev, g)
+        self.x = Shared((n * b, in_f), torch.int8, dev, g, ex.maps)
+        self.dy = Shared((n * b, out // n), torch.int8, dev, g, ex.maps)
+        self.w = Shared((out, in_f), torch.int8, dev, g, ex.maps)
         self.w.t.copy_(layer.w_i8)
         layer._buffers["w_i8"] = self.w.t  # the weights live in the shared buffer from now on
         self.layer = weakref.ref(layer)
@@ -89,15 +114,8 @@ class Exchange:
         if self.n > MAX_PEERS:
             raise RuntimeError(f"the peer exchange supports up to {MAX_PEERS} ranks")
         self.dev = device
-        from torch.distributed import _symmetric_memory as symm
-
-        if hasattr(symm, "enable_symm_mem_for_group") and not symm.is_symm_mem_enabled_for_group(group.group_name):
-            import warnings
-
-            with warnings.catch_warnings():  # needed by older torch releases, a no-op that warns in newer ones
-                warnings.simplefilter("ignore", FutureWarning)
-                symm.enable_symm_mem_for_group(group.group_name)
-        self.flags = Shared((MAX_SLOTS, MAX_PEERS), torch.int64, device, group)
+        self.maps = IpcMaps()
+        self.flags = Shared((MAX_SLOTS, MAX_PEERS), torch.int64, device, group, self.maps)
         self.flags.t.zero_()
         torch.cuda.synchronize(device)
         dist.barrier(group=group)  # every rank's flags are zero before anyone signals
@@ -107,7 +125,7 @@ class Exchange:
         self.dw = torch.cuda.Stream(device)
         self._ev = torch.cuda.Event()  # reused: orders the communication stream after the current one
         self.tickets = torch.zeros(MAX_SLOTS, dtype=torch.int32, device=device)  # push-and-signal tickets
-        self.red = Shared((2, self.n, RED_STRIDE), torch.int64, device, group)  # small all-reduce areas
+        self.red = Shared((2, self.n, RED_STRIDE), torch.int64, device, group, self.maps)  # small all-reduce areas
         self.red_ptrs = _arr(self.red.ptrs)
         self.layers: dict[int, LayerBufs] = {}
 
@@ -178,11 +196,15 @@ class Exchange:
         self.wait(bufs.slot_w, torch.cuda.current_stream(self.dev))
 
     def release(self) -> None:
-        """Give every layer a private copy of its weights again."""
+        """Give every layer a private copy of its weights again and unmap the peers'
+        buffers.  Collective: no rank frees a buffer before every rank has unmapped it."""
         torch.cuda.synchronize(self.dev)
         for bufs in self.layers.values():
             layer = bufs.layer()
             if layer is not None and layer._buffers.get("w_i8") is bufs.w.t:
                 layer._buffers["w_i8"] = bufs.w.t.clone()
         torch.cuda.synchronize(self.dev)
+        dist.barrier(group=self.group)  # every rank's kernels on the mapped buffers are done
+        self.maps.close_all()
+        dist.barrier(group=self.group)  # every rank has unmapped: the buffers may be freed
         self.layers.clear()

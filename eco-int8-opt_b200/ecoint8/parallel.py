@@ -294,6 +294,16 @@ def start_max(amax: torch.Tensor):
     return t, dist.all_reduce(t, op=dist.ReduceOp.MAX, group=_SMALL, async_op=True)
 
 
+def max_over_ranks(t: torch.Tensor) -> torch.Tensor:
+    """MAX over ranks of a short int32/int64 device vector, as int64, queued on the
+    current stream (the peer exchange's kernel, else NCCL); the host does not wait."""
+    if _PEER is not None:
+        return _PEER.allreduce(t.reshape(-1), "max")
+    out = t.reshape(-1).to(torch.int64)
+    dist.all_reduce(out, op=dist.ReduceOp.MAX, group=_SMALL if _SMALL is not None else _GROUP)
+    return out
+
+
 def _small_reduce(t: torch.Tensor, op: str) -> torch.Tensor:
     """MAX / SUM over ranks of a short vector (the peer exchange's kernel, else NCCL in place)."""
     if _PEER is not None and t.numel() <= 1024:

@@ -60,3 +60,71 @@ def saturation_ratio(q: torch.Tensor) -> float:
 
 def is_dead_grad(q: torch.Tensor) -> bool:
     return bool((q == 0).all())
+
+
+def cross_entropy_grad_i8(logits_i8: torch.Tensor, s_out, labels: torch.Tensor, count: int | None = None,
+                          return_fp32: bool = False):
+    """The strict loop's loss boundary in two kernels, with no host synchronisation.
+
+    Replaces, on CUDA tensors, the reference training loop's
+
+        logits_fp = (logits_i8.to(torch.float32) * s_out).requires_grad_()
+        loss = nn.CrossEntropyLoss()(logits_fp, y)
+        (g_fp,) = torch.autograd.grad(loss, logits_fp)
+        g_i8, s_g = quantize_tensor_dynamic(g_fp, stochastic=True)
+
+    (examples/i8_demo.py:56-59, quant.py:19-38).  Returns ``(loss, g_i8, s_g)``:
+    ``loss`` a 0-dim fp32 device tensor (the mean over ``count`` samples of this
+    process's rows), ``g_i8`` int8 ``[rows, cols]`` and ``s_g`` a device scale that
+    ``I8Sequential.backward_i8`` reads in place (``float(s_g)`` reads it on the host).
+
+    ``count``: the samples the mean runs over (default: the rows here; the global
+    batch under data parallelism, where max |g| is also taken over all ranks).
+    Stochastic rounding: the library's Philox stream with batch rows numbered
+    globally (``ecoint8._sr.batch_rows``), or, inside ``ecoint8.sr_replay()``, one
+    ``torch.rand`` draw of the logits' shape on their device -- the draw
+    ``torch.rand_like`` makes in the reference.  The fp32 gradient agrees with
+    PyTorch's to within a few ulp (its log-sum order is this kernel's own); given
+    the gradient, the quantization is PyTorch's arithmetic bit for bit.
+    ``return_fp32`` (tests): also return the fp32 gradient.
+    """
+    from . import _native as nat
+    from . import _scale, _sr, parallel
+
+    nat.require_cuda(logits_i8, labels)
+    if logits_i8.dtype != torch.int8 or logits_i8.dim() != 2:
+        raise AssertionError("logits must be a 2-D int8 tensor")
+    if labels.dtype != torch.int64 or labels.dim() != 1 or labels.shape[0] != logits_i8.shape[0]:
+        raise AssertionError("labels must be int64 [rows]")
+    x = logits_i8 if logits_i8.stride(1) == 1 else logits_i8.contiguous()
+    labels = labels.contiguous()
+    rows, cols = x.shape
+    ld = x.stride(0) if rows > 1 else cols
+    count = rows if count is None else int(count)
+    dev = x.device
+    s_out = float(s_out)
+    stats = torch.empty((rows, 2), dtype=torch.float32, device=dev)
+    row_loss = torch.empty(rows, dtype=torch.float32, device=dev)
+    amax = torch.empty(1, dtype=torch.int32, device=dev)
+    nat.call("eco_ce_grad_rowstats", x.data_ptr(), rows, cols, ld, s_out, labels.data_ptr(), count,
+             stats.data_ptr(), row_loss.data_ptr(), amax.data_ptr(), nat.stream())
+    amax_src, bits = amax, 32
+    if parallel.active():
+        amax_src, bits = parallel.max_over_ranks(amax), 64
+    keep = None
+    if _sr.replaying():
+        keep = torch.rand((rows, cols), device=dev)  # the reference's torch.rand_like(v) draw
+        spec = nat.sr_spec(nat.SR_REPLAY_F32, keep)
+    else:
+        spec = nat.sr_spec(nat.SR_PHILOX, seed=_sr.new_key(), stream_id=0, row_base=_sr.row_base())
+        if _sr.LOG is not None:
+            _sr.LOG.append(("boundary", spec.seed, 0, (rows, cols), 24, spec.row_base))
+    g = torch.empty((rows, cols), dtype=torch.int8, device=dev)
+    g_fp = torch.empty((rows, cols), dtype=torch.float32, device=dev) if return_fp32 else None
+    scale = torch.empty(3, dtype=torch.int64, device=dev)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    nat.call("eco_ce_grad_quantize", x.data_ptr(), rows, cols, ld, s_out, labels.data_ptr(), count,
+             stats.data_ptr(), amax_src.data_ptr(), bits, spec, g.data_ptr(), cols, nat.ptr(g_fp), scale.data_ptr(),
+             row_loss.data_ptr(), loss.data_ptr(), nat.stream())
+    s_g = _scale.DevScale(scale)
+    return (loss, g, s_g, g_fp) if return_fp32 else (loss, g, s_g)

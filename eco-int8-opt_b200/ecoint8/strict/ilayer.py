@@ -306,6 +306,7 @@ class I8Linear(nn.Module):
         x_i8 = self._cache_x
         assert isinstance(self.sx, float)
         s_x = self.sx
+        s_g = _scale.as_float(s_g)  # a device scale (the fused loss boundary's) is read here
         dev = _native.require_cuda(g_i8, x_i8, self.w_i8)
         N, out = g_i8.shape
         in_f = x_i8.shape[1]

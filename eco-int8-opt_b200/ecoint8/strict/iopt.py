@@ -31,6 +31,7 @@ from __future__ import annotations
 import ctypes
 import math
 import struct
+import time
 
 import torch
 
@@ -44,6 +45,7 @@ layer_values = _ScaleList.values
 __all__ = ["I8ECO"]
 
 FRAC_BITS = 12
+HOST_WAIT_S = [0.0]  # seconds step() spent waiting for the device (the previous step's flags)
 BETA_Q = 1 << 16  # beta in 16-bit fixed-point
 LR_Q = 1 << 16  # lr in 16-bit fixed-point (requires lr < 2)
 
@@ -206,7 +208,9 @@ class I8ECO:
     # -- step ------------------------------------------------------------
     @torch.no_grad()
     def step(self):
+        t0 = time.perf_counter()
         self._raise_pending(block=True)  # the previous step's flags (long since copied back)
+        HOST_WAIT_S[0] += time.perf_counter() - t0
         b = self.beta
         alpha = (1.0 / self.lr) * (1.0 - 1.0 / b)
         b_q = round(b * BETA_Q)
@@ -296,7 +300,9 @@ class I8ECO:
             self._flag_turn = 0
         flags, sflags, ev = self._flag_bufs[self._flag_turn]
         self._flag_turn ^= 1
+        t0 = time.perf_counter()
         ev.synchronize()  # its previous copy finished a step ago
+        HOST_WAIT_S[0] += time.perf_counter() - t0
         flags.copy_(self._state[:, 2], non_blocking=True)
         sflags.copy_(_scale.flags(dev), non_blocking=True)
         ev.record()

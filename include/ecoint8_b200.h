@@ -9,6 +9,14 @@
  * (a cudaStream_t; NULL = the legacy default stream).  After a failure,
  * eco_last_error() returns a message for the calling thread.
  *
+ * Process-wide state (everything else is per call):
+ *   - the GEMM CTA cap set by eco_set_gemm_sm_limit (default 0: one CTA per SM);
+ *   - a sticky device error word per GPU, set by bounded device waits that gave
+ *     up and read-and-cleared by eco_read_device_errors;
+ *   - the 32 MiB file-scope relayout buffer of eco_gemm_s8s32_noalloc (and its
+ *     cached device address, one per device);
+ *   - the IPC mappings a caller opened with eco_ipc_open, until eco_ipc_close.
+ *
  * Matrices are row-major with an explicit leading dimension in elements.
  * Stochastic rounding (SR) draws follow the caller's eco_sr_t:
  *   ECO_SR_NEAREST  round half up: nudge = 2^(shift-1)      (fixedpoint.py:72-73)
@@ -46,7 +54,9 @@ enum {
   ECO_ERR_RANGE = -5,       /* a requant shift outside [-63, 62] */
 };
 
-enum { ECO_SR_NEAREST = 0, ECO_SR_PHILOX = 1, ECO_SR_REPLAY32 = 2, ECO_SR_REPLAY64 = 3 };
+/* ECO_SR_REPLAY_F32: fp32 uniforms in [0, 1) at nudge[row * nudge_ld + col] (a
+ * torch.rand_like draw, quant.py:25); only the loss-boundary entry point takes it. */
+enum { ECO_SR_NEAREST = 0, ECO_SR_PHILOX = 1, ECO_SR_REPLAY32 = 2, ECO_SR_REPLAY64 = 3, ECO_SR_REPLAY_F32 = 4 };
 
 typedef void* eco_stream_t; /* cudaStream_t */
 
@@ -89,8 +99,10 @@ ECO_API int eco_gemm_s8s32(const int8_t* A, int64_t lda, int a_layout, const int
  * never into memory the call allocates.  A relayout larger than 32 MiB is
  * rejected with ECO_ERR_ARG.  All calls share that buffer, so calls that
  * overlap on the GPU race; the first call on a device looks the buffer up and
- * should come before any stream capture.  No counterpart in the reference
- * (its torch._int_mm path pads into freshly allocated tensors). */
+ * should come before any stream capture.  The looked-up address stays cached for
+ * the lifetime of the device's primary context: after cudaDeviceReset on a device,
+ * do not call this entry point on it again in that process.  No counterpart in the
+ * reference (its torch._int_mm path pads into freshly allocated tensors). */
 ECO_API int eco_gemm_s8s32_noalloc(const int8_t* A, int64_t lda, int a_layout, const int8_t* B,
                                    int64_t ldb, int b_layout, int64_t M, int64_t N, int64_t K,
                                    const int32_t* bias, int32_t* C, int64_t ldc, int32_t* amax,
@@ -155,6 +167,34 @@ ECO_API int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_
  * data parallelism). */
 ECO_API int eco_split_cols_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int64_t parts,
                       int8_t* dst, eco_stream_t stream);
+
+/* ------------------------------------------------------------ loss boundary -----
+ * The fp32 boundary at the end of the strict forward, fused into two launches with no
+ * host synchronisation.  Replaces the training loop's loss lines (examples/i8_demo.py:
+ * 56-59: logits_i8.float() * s_out, CrossEntropyLoss, its gradient) and the gradient's
+ * quantize_tensor_dynamic(g, stochastic=True) (quant.py:19-38 with its .item() amax).
+ * logits: [rows, cols] int8 (leading dim ld); labels: [rows] int64 in [0, cols); count:
+ * the number of samples the mean runs over (the global batch under data parallelism).
+ *
+ * eco_ce_grad_rowstats: per row (max, log-sum-exp) into row_stats [rows, 2] fp32, the
+ * row's NLL into row_loss [rows] (nullable), and *amax (overwritten) = the bit pattern
+ * of max |g| as an int32 (non-negative floats order like their bits, so a MAX over
+ * ranks of this word is the global maximum).
+ *
+ * eco_ce_grad_quantize: s_g = calc_scale(max|g|) with the maximum read from amax
+ * (int32 or int64 word holding the float's bits); g_i8 = clamp(floor(g * fp32(1 /
+ * (s_g + 1e-8)) + u), +-127) with u from sr (ECO_SR_PHILOX: 24 bits of the element's
+ * Philox field, or ECO_SR_REPLAY_F32).  scale_out: int64[3] = {double bits of s_g, 0, 0}
+ * (the layout of eco_scale_from_amax, so the queued backward reads it in place).
+ * g_fp (nullable): the fp32 gradient [rows, cols] as well.  loss_out (nullable, needs
+ * row_loss): sum of the row losses / count. */
+ECO_API int eco_ce_grad_rowstats(const int8_t* logits, int64_t rows, int64_t cols, int64_t ld, double s_out,
+                                 const int64_t* labels, int64_t count, float* row_stats, float* row_loss,
+                                 int32_t* amax, eco_stream_t stream);
+ECO_API int eco_ce_grad_quantize(const int8_t* logits, int64_t rows, int64_t cols, int64_t ld, double s_out,
+                                 const int64_t* labels, int64_t count, const float* row_stats, const void* amax,
+                                 int amax_bits, eco_sr_t sr, int8_t* g, int64_t ld_g, float* g_fp,
+                                 int64_t* scale_out, const float* row_loss, float* loss_out, eco_stream_t stream);
 
 /* ---------------------------------------------- device-side scales -----
  * The backward's dynamic scale chain without host round trips (used when a whole
@@ -227,6 +267,18 @@ ECO_API int eco_peer_signal(int64_t* const* peer_flags, int n, int rank, int slo
                     eco_stream_t stream);
 ECO_API int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, int64_t timeout_us,
                   eco_stream_t stream);
+
+/* Mapping the exchange buffers between the processes of one node (CUDA IPC).
+ * export: the IPC handle (ECO_IPC_HANDLE_BYTES bytes at `handle`) of the device
+ * allocation that contains `ptr`, and ptr's byte offset in it; the caller sends both
+ * to the other ranks.  open: maps a peer's allocation into this process (unicast peer
+ * mapping over NVLink; no multicast object is created) and returns its base; the
+ * peer's buffer is base + offset.  close: unmaps a base returned by open.  The
+ * exporting rank must keep its allocation alive until every peer has closed it. */
+#define ECO_IPC_HANDLE_BYTES 64
+ECO_API int eco_ipc_export(const void* ptr, void* handle, int64_t* offset);
+ECO_API int eco_ipc_open(const void* handle, void** base);
+ECO_API int eco_ipc_close(void* base);
 
 /* -------------------------------------------------------- I8ECO step -----
  * One fused, single-pass integer ECO-SGDM step over a list of layers

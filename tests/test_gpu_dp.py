@@ -5,9 +5,11 @@ through NCCL; the same through the library's NVLink peer stores).
 Two ranks split a batch of 96 rows; rank 0 also trains an identical net on the
 whole batch on its own.  Both use the same Philox key sequence, so after
 several training steps every weight, momentum, bias and momentum scale must
-agree exactly.  The fp32 loss boundary is made deterministic (round-to-nearest
-quantization of the gradient on its global scale) so both sides feed the same
-int8 gradient.  Skipped with fewer than 2 GPUs.
+agree exactly.  The fp32 loss boundary is either made deterministic (round-to-nearest
+quantization of the gradient on its global scale) or is the fused boundary
+(``cross_entropy_grad_i8``: global maximum over the ranks, Philox uniforms on
+global rows), so both sides feed the same int8 gradient.  Skipped with fewer
+than 2 GPUs.
 """
 
 import datetime
@@ -53,9 +55,10 @@ def _boundary(logits, s_out, y, world):
     return quantize_symmetric(g, s, stochastic=False), s
 
 
-def _train(net, x8, sx, y, world, row_base, gen_seed, steps):
+def _train(net, x8, sx, y, world, row_base, gen_seed, steps, fused=False):
     from ecoint8 import I8ECO
     from ecoint8._sr import batch_rows, set_generator
+    from ecoint8.quant import cross_entropy_grad_i8
 
     set_generator(torch.Generator().manual_seed(gen_seed))
     with batch_rows(row_base):
@@ -63,7 +66,10 @@ def _train(net, x8, sx, y, world, row_base, gen_seed, steps):
         opt = I8ECO(net.int8_layers(), lr=0.3, momentum=0.9)
         for _ in range(steps):
             logits, s_out = net.forward_i8(x8)
-            g8, sg = _boundary(logits, s_out, y, world)
+            if fused:
+                _, g8, sg = cross_entropy_grad_i8(logits, s_out, y, count=B)
+            else:
+                g8, sg = _boundary(logits, s_out, y, world)
             net.backward_i8(g8, sg)
             opt.step()
             opt.zero_grad()
@@ -92,19 +98,19 @@ def _worker(rank, port, q):
         X8, sx = quantize_tensor_dynamic(X)  # entry scale of the global batch, identical on both ranks
         lo, hi = rank * B // 2, (rank + 1) * B // 2
         runs = {}
-        for exchange in ("reduce", "gather", "peer"):
+        for exchange, fused in (("reduce", False), ("gather", False), ("peer", False), ("peer", True)):
             parallel.init(dw_exchange=exchange)
             net = _net(dev)
-            opt = _train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), 2, lo, 123, 4)
+            opt = _train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), 2, lo, 123, 4, fused)
             parallel.synchronize(net.int8_layers())  # the last step's row all-gathers
             parallel.gather_momentum(opt)  # momentum rows live on their owner rank
-            runs[exchange] = (net, opt, opt.stats["mean_abs_e"])
+            runs[exchange + ("+fused" if fused else "")] = (net, opt, opt.stats["mean_abs_e"])
             parallel.shutdown()
         if rank == 0:
-            single = _net(dev)
-            sopt = _train(single, X8.to(dev), sx, Y.to(dev), 1, 0, 123, 4)
             res = {}
             for exchange, (net, opt, stats) in runs.items():
+                single = _net(dev)
+                sopt = _train(single, X8.to(dev), sx, Y.to(dev), 1, 0, 123, 4, exchange.endswith("+fused"))
                 ok = all(torch.equal(a.w_i8, b.w_i8) for a, b in zip(net.int8_layers(), single.int8_layers()))
                 ok &= all(torch.equal(a.b_acc, b.b_acc) for a, b in zip(net.int8_layers(), single.int8_layers()))
                 ok &= all(torch.equal(a, b) for a, b in zip(opt.m_i8, sopt.m_i8))
@@ -136,4 +142,4 @@ def test_two_gpu_data_parallel_equals_single_gpu():
     for p in ps:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert ok == {"reduce": True, "gather": True, "peer": True}
+    assert ok == {"reduce": True, "gather": True, "peer": True, "peer+fused": True}
