@@ -100,6 +100,22 @@ def mnist_batch(index: int, batch: int = MNIST_B):
     return X, y
 
 
+MNIST_GOLDEN_STEPS = 100  # steps of the MNIST-shaped run pinned by the golden fixture
+
+WIDE_D, WIDE_C, WIDE_B = 8192, 1000, 64  # config-5 layer widths, the golden fixture's batch
+
+
+def wide_batch():
+    """Config-5-shaped inputs: Gaussian features ``[64, 8192]`` and labels uniform over 1000
+    classes, from their own generator (seed 2000)."""
+    import torch
+
+    gen = torch.Generator().manual_seed(2000)
+    X = torch.randn(WIDE_B, WIDE_D, generator=gen)
+    y = torch.randint(0, WIDE_C, (WIDE_B,), generator=gen)
+    return X, y
+
+
 def mnist_lr(step: int, total: int, lr0: float = 0.08) -> float:
     """Cosine lr over ``total`` steps (lr0 = 0.08 as in examples/mem_probe.py:83)."""
     return lr0 * 0.5 * (1 + math.cos(math.pi * step / total)) + 1e-4

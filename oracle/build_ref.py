@@ -3,9 +3,10 @@
     python oracle/build_ref.py [--reference DIR]      (default: $ECOINT8_REFERENCE)
 
 The reference (eco-int8-opt 0.4.9) is pure Python on PyTorch.  This recipe
-byte-compiles its ``ecoint8`` package where it lies into sourceless bytecode under
-``oracle/_ref/ecoint8/`` (one ``.pyc`` per module, importable without the sources;
-the GPU machines run the same Python version).  No source file is copied.
+byte-compiles its ``ecoint8`` package where it lies into sourceless bytecode, one
+compiled module per source module, stored in the archive ``oracle/_ref/ecoint8.zip``
+(importable without the sources through Python's zip importer; the GPU machines run
+the same Python version).  No source file is copied.
 ``bench.py`` imports the package from there to time the reference's own strict
 step on the host cores: the ``--impl reference`` arm and ``cpu_baseline``.
 ``oracle/_ref`` is listed in ``.gitignore`` and is never committed.
@@ -14,14 +15,16 @@ step on the host cores: the ``--impl reference`` arm and ``cpu_baseline``.
 from __future__ import annotations
 
 import argparse
+import importlib.util
+import marshal
 import os
 import pathlib
-import py_compile
-import shutil
 import sys
+import zipfile
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref"
+ARCHIVE = OUT / "ecoint8.zip"
 
 
 def build(reference: str | os.PathLike | None = None) -> pathlib.Path | None:
@@ -32,16 +35,19 @@ def build(reference: str | os.PathLike | None = None) -> pathlib.Path | None:
     pkg = pathlib.Path(ref) / "ecoint8"
     if not (pkg / "__init__.py").exists():
         raise FileNotFoundError(f"no ecoint8 package under {ref}")
-    dst_root = OUT / "ecoint8"
-    if dst_root.exists():
-        shutil.rmtree(dst_root)
-    for src in sorted(pkg.rglob("*.py")):
-        rel = src.relative_to(pkg)
-        dst = dst_root / rel.with_suffix(".pyc")
-        dst.parent.mkdir(parents=True, exist_ok=True)
-        py_compile.compile(str(src), cfile=str(dst), dfile=f"ecoint8/{rel}", doraise=True)
+    OUT.mkdir(exist_ok=True)
+    tmp = ARCHIVE.with_suffix(".tmp")
+    with zipfile.ZipFile(tmp, "w", zipfile.ZIP_DEFLATED) as z:
+        for src in sorted(pkg.rglob("*.py")):
+            rel = src.relative_to(pkg)
+            code = compile(src.read_bytes(), f"ecoint8/{rel}", "exec", dont_inherit=True)
+            # a sourceless .pyc: magic, flags 0 (timestamp-based), mtime, size, marshalled code
+            head = importlib.util.MAGIC_NUMBER + (0).to_bytes(4, "little") + (0).to_bytes(4, "little") \
+                + (0).to_bytes(4, "little")
+            z.writestr(str(pathlib.PurePosixPath("ecoint8", rel.with_suffix(".pyc"))), head + marshal.dumps(code))
+    os.replace(tmp, ARCHIVE)
     (OUT / "BUILT_FROM").write_text(f"{pkg.resolve()}\npython {sys.version.split()[0]}\n")
-    return OUT
+    return ARCHIVE
 
 
 def load():
@@ -51,19 +57,19 @@ def load():
     need the sources that the bytecode build does not carry (the reference then takes
     its own CPU-install branch, ``TRITON_AVAILABLE = False``).
     """
-    if not (OUT / "ecoint8" / "__init__.pyc").exists():
+    if not ARCHIVE.exists():
         return None
     if "ecoint8" in sys.modules and not getattr(sys.modules["ecoint8"], "__file__", "").startswith(str(OUT)):
         raise RuntimeError("another ecoint8 package is already imported in this process")
     sys.modules.setdefault("triton", None)
-    sys.path.insert(0, str(OUT))
+    sys.path.insert(0, str(ARCHIVE))
     try:
         import ecoint8  # noqa: F401
         import ecoint8.strict as strict
         import ecoint8.quant as quant
     finally:
-        sys.path.remove(str(OUT))
-    assert pathlib.Path(ecoint8.__file__).resolve().is_relative_to(OUT.resolve())
+        sys.path.remove(str(ARCHIVE))
+    assert ecoint8.__file__.startswith(str(ARCHIVE))
     return {"ecoint8": ecoint8, "strict": strict, "quant": quant, "version": ecoint8.__version__}
 
 

@@ -56,12 +56,51 @@ def _words(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray, per: int)
     return cols, x
 
 
+def _full_width(rows, cols):
+    """``(row column vector, n)`` when ``cols`` is the row vector ``0 .. n-1`` (a whole-width
+    block, where one Philox call per counter serves all its columns), else None."""
+    r = np.asarray(rows)
+    c = np.asarray(cols)
+    if c.ndim == 2 and c.shape[0] == 1 and r.ndim == 2 and r.shape[1] == 1 and c.shape[1] > 0:
+        n = c.shape[1]
+        if c[0, 0] == 0 and c[0, -1] == n - 1 and np.array_equal(c[0], np.arange(n, dtype=c.dtype)):
+            return r.astype(np.uint64), n
+    return None
+
+
+def _interleave(words, n):
+    """Words ``[rows, calls]`` each -> ``[rows, len(words) * calls]``, call-major, cut to ``n`` columns."""
+    out = np.stack(words, axis=-1)
+    return out.reshape(out.shape[0], -1)[:, :n]
+
+
+def _blocks(r, calls: int, n: int, fn):
+    """``fn(row block, call indices)`` -> its ``[block rows, n]`` words, over blocks of about
+    256 K calls (numpy temporaries that stay in cache)."""
+    out = np.empty((r.shape[0], n), dtype=np.uint64)
+    idx = np.arange(calls, dtype=np.uint64)[None, :]
+    step = max(1, (1 << 18) // max(calls, 1))
+    for i in range(0, r.shape[0], step):
+        out[i:i + step] = fn(r[i:i + step], idx)
+    return out
+
+
 def sr_word(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
     """64 random bits for element ``(row, col)`` of site ``stream`` (uint64).
 
     Counter ``(col >> 1, row, stream_lo, stream_hi)``, key ``(seed_lo, seed_hi)``;
     an even column takes words ``(x1:x0)``, an odd column ``(x3:x2)``.
     """
+    fw = _full_width(rows, cols)
+    if fw is not None:  # one call per column pair
+        r, n = fw
+
+        def words(rb, pairs):
+            x0, x1, x2, x3 = philox4x32(pairs, rb, stream & 0xFFFFFFFF, (stream >> 32) & 0xFFFFFFFF,
+                                        seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)
+            return _interleave([(x1 << np.uint64(32)) | x0, (x3 << np.uint64(32)) | x2], n)
+
+        return _blocks(r, (n + 1) // 2, n, words)
     cols, (x0, x1, x2, x3) = _words(seed, stream, rows, cols, 2)
     lo = np.where((cols & np.uint64(1)) == 0, x0, x2)
     hi = np.where((cols & np.uint64(1)) == 0, x1, x3)
@@ -70,6 +109,15 @@ def sr_word(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.nd
 
 def sr_field(seed: int, stream: int, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
     """32 random bits for element ``(row, col)``: word ``col & 3`` of counter ``(col >> 2, row, stream)``."""
+    fw = _full_width(rows, cols)
+    if fw is not None:  # one call per column quad
+        r, n = fw
+
+        def words(rb, quads):
+            return _interleave(list(philox4x32(quads, rb, stream & 0xFFFFFFFF, (stream >> 32) & 0xFFFFFFFF,
+                                               seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)), n)
+
+        return _blocks(r, (n + 3) // 4, n, words)
     cols, (x0, x1, x2, x3) = _words(seed, stream, rows, cols, 4)
     k = cols & np.uint64(3)
     return np.select([k == 0, k == 1, k == 2], [x0, x1, x2], x3).astype(np.uint64)

@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout exists (read-only is fine)::
 
-    python tests/golden/make_golden.py --reference /root/reference
+    ECOINT8_REFERENCE=<checkout> python tests/golden/make_golden.py [--only NAME.json ...]
 
 It imports the reference package from that path, runs the seeded workloads of
 ``oracle/boundary.py`` through the reference's own public API on CPU, and writes
@@ -213,6 +213,42 @@ def gen_mnist(ref, bnd, nsteps):
     return {"steps": steps}
 
 
+def gen_wide(ref, bnd, nsteps: int):
+    """Config-5 widths: I8Linear(8192, 8192) + I8ReLU + I8Linear(8192, 1000) at batch 64,
+    Gaussian inputs quantized with the calibrated entry scale, random labels, I8ECO lr 0.05
+    momentum 0.9; digests after every step."""
+    import torch
+
+    I8Linear, I8ReLU, I8Sequential, I8ECO = (ref["I8Linear"], ref["I8ReLU"], ref["I8Sequential"],
+                                             ref["I8ECO"])
+    torch.manual_seed(0)
+    net = I8Sequential(I8Linear(bnd.WIDE_D, bnd.WIDE_D), I8ReLU(), I8Linear(bnd.WIDE_D, bnd.WIDE_C))
+    X, y = bnd.wide_batch()
+    with torch.no_grad():
+        x0, sx0 = bnd.quantize_tensor_dynamic(X, stochastic=False)
+        cal, _ = net.calibrate(x0, sx0)
+        x_i8, _ = net.quantize_input(X)
+    opt = I8ECO(net.int8_layers(), lr=0.05, momentum=0.9)
+    steps = []
+    for _ in range(nsteps):
+        with DrawLog(ref["fixedpoint"], ref["iopt"]) as dl:
+            with torch.no_grad():
+                logits, s_out = net.forward_i8(x_i8)
+            loss, g_fp = bnd.ce_grad(logits, s_out, y)
+            g_i8, s_g = bnd.quantize_tensor_dynamic(g_fp, stochastic=True)
+            with torch.no_grad():
+                net.backward_i8(g_i8, s_g)
+            gws = [{"gw": digest(l._gw_i8), "gw_s": fhex(l._gw_s), "gb": digest(l._gb_sum)}
+                   for l in net.int8_layers()]
+            opt.step()
+            opt.zero_grad()
+        steps.append({"logits": digest(logits), "s_out": fhex(s_out), "g": digest(g_i8), "s_g": fhex(s_g),
+                      "grads": gws, "layers": layer_state(net, opt), "mean_abs_e": fhex(opt.stats["mean_abs_e"]),
+                      "draws": dl.log})
+    return {"init": [digest(l.w_i8) for l in net.int8_layers()], "calib": digest(cal),
+            "sy": [fhex(l.sy) for l in net.int8_layers()], "x_i8": digest(x_i8), "steps": steps}
+
+
 def gen_gemm_requant(ref):
     import torch
 
@@ -310,9 +346,13 @@ def gen_sgdm_triton(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ECOINT8_REFERENCE"),
+                    help="the reference checkout (default: $ECOINT8_REFERENCE)")
     ap.add_argument("--epochs", type=int, default=150)
+    ap.add_argument("--only", nargs="*", default=None, help="fixture file names to (re)generate")
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("give --reference or set ECOINT8_REFERENCE")
     os.environ["TRITON_INTERPRET"] = "1"
     sys.path.insert(0, str(REPO))
     sys.path.insert(0, args.reference)
@@ -330,14 +370,18 @@ def main():
     ref = {"fixedpoint": fixedpoint, "ilayer": ilayer, "iopt": iopt, "triton_kernels": triton_kernels,
            "I8Linear": ilayer.I8Linear, "I8ReLU": ilayer.I8ReLU, "I8Sequential": ilayer.I8Sequential,
            "I8ECO": iopt.I8ECO}
-    fixtures = {
-        "fixedpoint.json": gen_fixedpoint(ref),
-        "blob_train.json": gen_blob(ref, bnd, args.epochs),
-        "mnist_train.json": gen_mnist(ref, bnd, 3),
-        "gemm_requant.json": gen_gemm_requant(ref),
-        "eco_step.json": gen_eco_step(ref),
-        "sgdm_triton.json": gen_sgdm_triton(ref),
+    gens = {
+        "fixedpoint.json": lambda: gen_fixedpoint(ref),
+        "blob_train.json": lambda: gen_blob(ref, bnd, args.epochs),
+        "mnist_train.json": lambda: gen_mnist(ref, bnd, bnd.MNIST_GOLDEN_STEPS),
+        "gemm_requant.json": lambda: gen_gemm_requant(ref),
+        "eco_step.json": lambda: gen_eco_step(ref),
+        "sgdm_triton.json": lambda: gen_sgdm_triton(ref),
+        "wide_train.json": lambda: gen_wide(ref, bnd, 2),
     }
+    if args.only:
+        torch.set_num_threads(os.cpu_count() or 1)  # the wide fixture's GEMMs (results do not depend on it)
+    fixtures = {name: fn() for name, fn in gens.items() if not args.only or name in args.only}
     meta = {"reference": "valik8937/eco-int8-opt", "version": ecoint8.__version__,
             "torch": torch.__version__, "generator": "tests/golden/make_golden.py"}
     for name, obj in fixtures.items():
