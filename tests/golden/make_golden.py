@@ -223,6 +223,7 @@ def gen_wide(ref, bnd, nsteps: int):
                                              ref["I8ECO"])
     torch.manual_seed(0)
     net = I8Sequential(I8Linear(bnd.WIDE_D, bnd.WIDE_D), I8ReLU(), I8Linear(bnd.WIDE_D, bnd.WIDE_C))
+    init = [digest(l.w_i8) for l in net.int8_layers()]
     X, y = bnd.wide_batch()
     with torch.no_grad():
         x0, sx0 = bnd.quantize_tensor_dynamic(X, stochastic=False)
@@ -245,7 +246,7 @@ def gen_wide(ref, bnd, nsteps: int):
         steps.append({"logits": digest(logits), "s_out": fhex(s_out), "g": digest(g_i8), "s_g": fhex(s_g),
                       "grads": gws, "layers": layer_state(net, opt), "mean_abs_e": fhex(opt.stats["mean_abs_e"]),
                       "draws": dl.log})
-    return {"init": [digest(l.w_i8) for l in net.int8_layers()], "calib": digest(cal),
+    return {"init": init, "calib": digest(cal),
             "sy": [fhex(l.sy) for l in net.int8_layers()], "x_i8": digest(x_i8), "steps": steps}
 
 
