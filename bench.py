@@ -129,7 +129,7 @@ def _step_kernels(layers, n, *rest) -> int:
 
 # library kernels launched per C-ABI call (an int, or a function of the call's arguments)
 KERNELS_PER_CALL = {"eco_gemm_s8s32": 1, "eco_gemm_s8_requant": 1, "eco_requant_s32_s8": 1,
-                    "eco_requant_s32_s8_dev": 2, "eco_scale_from_amax": 1, "eco_apply_mult_shift": 1,
+                    "eco_requant_s32_s8_dev": 1, "eco_scale_from_amax": 1, "eco_apply_mult_shift": 1,
                     "eco_colsum_s8": 1, "eco_amax": 2, "eco_sumsq_s8": 1, "eco_split_cols_s8": 1,
                     "eco_i8eco_step": _step_kernels, "eco_i8eco_finalize": 1, "eco_sgdm_step": 3,
                     "eco_peer_push_s8": 1, "eco_peer_push_signal_s8": 1, "eco_peer_signal": 1,
@@ -589,6 +589,9 @@ def main():
     ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to the exchange under data parallelism")
     ap.add_argument("--push-ctas", type=int, default=32, help="CTAs per push kernel of the peer exchange")
     ap.add_argument("--trace", default=None, help="with --profile: write rank 0's chrome trace to this file")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="issue every step from the host (default: capture the step once as a CUDA graph, "
+                         "ecoint8.graphs.StepGraph, and replay it)")
     ap.add_argument("--profile", action="store_true",
                     help="after timing, run 3 steps under torch.profiler and print rank 0's GPU-time table")
     args = ap.parse_args()
@@ -643,8 +646,23 @@ def main():
             if world > 1:
                 torch.distributed.barrier()
 
-        for _ in range(args.warmup):
-            train_step(net, opt, x_i8, y)
+        graph = None
+        if args.no_graph:
+            for _ in range(args.warmup):
+                train_step(net, opt, x_i8, y)
+        else:
+            from ecoint8.graphs import StepGraph
+
+            # the first warm-up step runs eagerly inside capture(); the graph then holds
+            # exactly one step's launches, counted while it is recorded
+            graph = StepGraph(lambda: train_step(net, opt, x_i8, y), warmup=1)
+            counter = LaunchCounter()
+            with counter:
+                graph.capture()
+            graph_launches = counter.count // 2  # the eager warm-up step + the recorded step
+            for _ in range(args.warmup - 1):
+                graph.replay()
+        step = graph.replay if graph is not None else (lambda: train_step(net, opt, x_i8, y))
         torch.cuda.synchronize()
         barrier()
         counter = LaunchCounter()
@@ -656,14 +674,14 @@ def main():
             w0 = time.perf_counter()
             ev0.record()
             for _ in range(args.steps):
-                train_step(net, opt, x_i8, y)
+                step()
             ev1.record()
             host_wall = time.perf_counter() - w0
             host_blocked = iopt.HOST_WAIT_S[0]
             torch.cuda.synchronize()
             barrier()
         ms = ev0.elapsed_time(ev1)
-        launches = counter.count // args.steps
+        launches = graph_launches if graph is not None else counter.count // args.steps
         # e2e: the same steps through the public API with the int8 batch and labels coming
         # from pinned host memory and the loss read back every step; like a data loader,
         # the next step's batch crosses PCIe on a copy stream while this step computes
@@ -680,20 +698,47 @@ def main():
                 ev.record(copy_stream)
             return xb, yb, ev
 
+        # with a graph: the batch lands in one of two staging buffers while the previous
+        # step runs, and moves into the graph's input tensors at the start of its step
+        stage = [(torch.empty_like(x_i8), torch.empty_like(y)) for _ in range(2)] if graph is not None else None
+        used = [None, None]
+
+        def fetch_staged(i):
+            k = i % 2
+            if used[k] is not None:
+                copy_stream.wait_event(used[k])  # its last step has moved it into the inputs
+            with torch.cuda.stream(copy_stream):
+                stage[k][0].copy_(x_host, non_blocking=True)
+                stage[k][1].copy_(y_host, non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+            return ev
+
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         copy_stream.wait_event(e0)  # the first batch's copy is inside the timed region too
-        nxt = fetch()
+        nxt = fetch() if graph is None else fetch_staged(0)
         for i in range(args.steps):
-            xb, yb, ev = nxt
-            cur.wait_event(ev)
-            xb.record_stream(cur)
-            yb.record_stream(cur)
-            if i + 1 < args.steps:
-                nxt = fetch()
-            loss = train_step(net, opt, xb, yb)
+            if graph is None:
+                xb, yb, ev = nxt
+                cur.wait_event(ev)
+                xb.record_stream(cur)
+                yb.record_stream(cur)
+                if i + 1 < args.steps:
+                    nxt = fetch()
+                loss = train_step(net, opt, xb, yb)
+            else:
+                cur.wait_event(nxt)
+                x_i8.copy_(stage[i % 2][0])
+                y.copy_(stage[i % 2][1])
+                u = torch.cuda.Event()
+                u.record(cur)
+                used[i % 2] = u
+                if i + 1 < args.steps:
+                    nxt = fetch_staged(i + 1)
+                loss = graph.replay()
             if world > 1:
                 torch.distributed.all_reduce(loss)  # the mean over the global batch
             float(loss.item())
@@ -706,7 +751,7 @@ def main():
 
             with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
                 for _ in range(3):
-                    train_step(net, opt, x_i8, y)
+                    step()
                 torch.cuda.synchronize()
             if rank == 0:
                 print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70),
@@ -735,7 +780,7 @@ def main():
                           "data": "global batch drawn once from seed 100, rows split across ranks"},
                "e2e": {"value": e2e, "unit": "steps/s", "h2d_bytes_per_step": int(x_i8.numel() + y.numel() * 8),
                        "d2h_bytes_per_step": 4},
-               "gpu_launches": launches, "clocks": clk.summary(),
+               "gpu_launches": launches, "cuda_graph": graph is not None, "clocks": clk.summary(),
                "host": {"issue_ms_per_step": 1e3 * (host_wall - host_blocked) / args.steps,
                         "blocked_ms_per_step": 1e3 * host_blocked / args.steps},
                "weights_digest": digest}

@@ -29,8 +29,10 @@ int eco_num_sms() {
 int eco_check_sr(const eco_sr_t& sr, int shift, const char* who) {
   if (shift > 62)
     return eco_fail(ECO_ERR_RANGE, "%s: shift %d > 62 does not fit the int64 requant", who, shift);
-  if (sr.mode < ECO_SR_NEAREST || sr.mode > ECO_SR_REPLAY64)
+  if (sr.mode < ECO_SR_NEAREST || sr.mode > ECO_SR_PHILOX_DEV || sr.mode == ECO_SR_REPLAY_F32)
     return eco_fail(ECO_ERR_ARG, "%s: unknown SR mode %d", who, sr.mode);
+  if (sr.mode == ECO_SR_PHILOX_DEV && (sr.nudge == nullptr || (reinterpret_cast<uintptr_t>(sr.nudge) & 7) != 0))
+    return eco_fail(ECO_ERR_ARG, "%s: ECO_SR_PHILOX_DEV needs an 8-byte aligned key word", who);
   if ((sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64) && shift >= 0 && sr.nudge == nullptr)
     return eco_fail(ECO_ERR_ARG, "%s: replay SR mode without a nudge tensor", who);
   return ECO_OK;

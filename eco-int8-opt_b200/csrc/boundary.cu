@@ -140,12 +140,14 @@ __global__ void ce_quantize_kernel(const __grid_constant__ QuantArgs A) {
   const int8_t* row = A.L + r * A.ld;
   const float2 st = A.stats[r];
   const int64_t y = A.labels[r];
-  const bool philox = A.sr.mode == ECO_SR_PHILOX;
-  const uint32_t grow = (uint32_t)(A.sr.row_base + r);
+  PhiloxKeys keys;
+  const eco_sr_t sr = sr_resolve(A.sr, A.keys, keys);
+  const bool philox = sr.mode == ECO_SR_PHILOX;
+  const uint32_t grow = (uint32_t)(sr.row_base + r);
   int8_t* out = A.g + r * A.ld_g;
   for (int64_t j0 = 4 * lane; j0 < A.cols; j0 += 128) {
     Philox4 rnd{0u, 0u, 0u, 0u};
-    if (philox) rnd = sr_quad_k(A.keys, A.sr.stream, grow, (uint32_t)(j0 >> 2));
+    if (philox) rnd = sr_quad_k(keys, sr.stream, grow, (uint32_t)(j0 >> 2));
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
       const int64_t j = j0 + t;
@@ -153,7 +155,7 @@ __global__ void ce_quantize_kernel(const __grid_constant__ QuantArgs A) {
       const float g = ce_grad(logit(row, j, A.s), st.x, st.y, j == y, A.c);
       if (A.g_fp) A.g_fp[r * A.cols + j] = g;
       const float u = philox ? __fmul_rn((float)(quad_word(rnd, t) >> 8), 0x1p-24f)
-                             : static_cast<const float*>(A.sr.nudge)[r * A.sr.nudge_ld + j];
+                             : static_cast<const float*>(sr.nudge)[r * sr.nudge_ld + j];
       const float q = floorf(__fadd_rn(__fmul_rn(g, inv), u));
       out[j] = (int8_t)fmaxf(-127.0f, fminf(127.0f, q));
     }
@@ -186,7 +188,8 @@ extern "C" int eco_ce_grad_quantize(const int8_t* logits, int64_t rows, int64_t 
   ECO_REQUIRE(logits && labels && row_stats && amax && g && scale_out && rows >= 0 && cols > 0 && ld >= cols &&
                   ld_g >= cols && count > 0 && (amax_bits == 32 || amax_bits == 64),
               ECO_ERR_ARG, "eco_ce_grad_quantize: bad arguments");
-  ECO_REQUIRE(sr.mode == ECO_SR_PHILOX || (sr.mode == ECO_SR_REPLAY_F32 && sr.nudge && sr.nudge_ld >= cols),
+  ECO_REQUIRE(sr.mode == ECO_SR_PHILOX || (sr.mode == ECO_SR_PHILOX_DEV && sr.nudge) ||
+                  (sr.mode == ECO_SR_REPLAY_F32 && sr.nudge && sr.nudge_ld >= cols),
               ECO_ERR_ARG, "eco_ce_grad_quantize: SR mode must be Philox or fp32 replay");
   ECO_REQUIRE(!loss_out || row_loss, ECO_ERR_ARG, "eco_ce_grad_quantize: the loss needs the row losses");
   QuantArgs A;
@@ -201,7 +204,7 @@ extern "C" int eco_ce_grad_quantize(const int8_t* logits, int64_t rows, int64_t 
   A.amax = amax;
   A.amax_bits = amax_bits;
   A.sr = sr;
-  A.keys = philox_keys(sr.seed);
+  A.keys = philox_keys(sr.mode == ECO_SR_PHILOX ? sr.seed : 0);
   A.g = g;
   A.ld_g = ld_g;
   A.g_fp = g_fp;

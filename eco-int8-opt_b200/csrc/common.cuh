@@ -131,6 +131,25 @@ ECO_DEV Philox4 philox10k(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, co
   }
   return Philox4{c0, c1, c2, c3};
 }
+// A site as a kernel uses it: ECO_SR_PHILOX_DEV becomes ECO_SR_PHILOX with the key
+// read from device memory now (the launch may be a CUDA graph replay); `keys` gets the
+// site's round keys (the host-computed ones of a plain Philox site).
+ECO_DEV eco_sr_t sr_resolve(const eco_sr_t& in, const PhiloxKeys& host_keys, PhiloxKeys& keys) {
+  eco_sr_t sr = in;
+  if (sr.mode == ECO_SR_PHILOX_DEV) {
+    sr.seed = *static_cast<const u64*>(in.nudge);
+    sr.mode = ECO_SR_PHILOX;
+    sr.nudge = nullptr;
+    keys = philox_keys(sr.seed);
+  } else {
+    keys = host_keys;
+  }
+  return sr;
+}
+ECO_DEV eco_sr_t sr_resolve(const eco_sr_t& in) {
+  PhiloxKeys unused;
+  return sr_resolve(in, unused, unused);
+}
 // sr_quad with precomputed round keys (same bits).
 ECO_DEV Philox4 sr_quad_k(const PhiloxKeys& K, u64 stream, uint32_t row, uint32_t quad) {
   return philox10k(quad, row, (uint32_t)stream, (uint32_t)(stream >> 32), K);

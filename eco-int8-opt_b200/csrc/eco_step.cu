@@ -286,6 +286,33 @@ ECO_DEV int8_t m_requant(const RowCtx& c, i64 m_new, bool philox, uint32_t field
   return sat8(sar64(add64(prod, nm_replay), c.com_mm));
 }
 
+// The step's hyper-parameters and round keys as the launch sees them: the launch's
+// copy or, when it names one, the device copy of the moment (a CUDA graph replay).
+// Staged in shared memory by the block's first thread.
+struct StepShared {
+  eco_i8eco_hyper_t H;
+  PhiloxKeys keys;
+};
+ECO_DEV void stage_hyper(const StepParams& P, StepShared& sh) {
+  if (threadIdx.x == 0) {
+    sh.H = P.H;
+    if (P.H.dev) {
+      const eco_i8eco_hyper_t& D = *P.H.dev;
+      sh.H.lr = D.lr;
+      sh.H.grad_clip = D.grad_clip;
+      sh.H.b_q = D.b_q;
+      sh.H.nb_q = D.nb_q;
+      sh.H.lr_q = D.lr_q;
+      sh.H.a_q = D.a_q;
+      sh.H.seed = D.seed;
+      sh.keys = philox_keys(D.seed);
+    } else {
+      sh.keys = P.keys;
+    }
+  }
+  __syncthreads();
+}
+
 // Bias integer SGD of one row (iopt.py:187-197); r indexes the layer's arrays
 // (global row r + row_base).
 template <bool PHILOX>
@@ -307,14 +334,16 @@ ECO_DEV void bias_update(const eco_i8eco_layer_t& L, const eco_i8eco_hyper_t& H,
 // (the step kernel records the flags).
 template <bool PHILOX>
 __global__ void i8eco_bias_kernel(const __grid_constant__ StepParams P) {
+  __shared__ StepShared sh;
+  stage_hyper(P, sh);
   const eco_i8eco_layer_t& L = P.layers[blockIdx.y].L;
   const i64 R = (i64)blockIdx.x * blockDim.x + threadIdx.x;
   if (!L.b_acc || R >= L.bias_rows) return;
-  const LayerScalars S = layer_scalars(L, P.H);
+  const LayerScalars S = layer_scalars(L, sh.H);
   if (S.flags) return;
   const i64 r = R - L.row_base;
   unsigned flags = 0;
-  bias_update<PHILOX>(L, P.H, S, r, L.sw[r], flags);
+  bias_update<PHILOX>(L, sh.H, S, r, L.sw[r], flags);
   if (flags) atomicOr(reinterpret_cast<unsigned long long*>(&L.state[2]), (u64)flags);
 }
 
@@ -322,8 +351,10 @@ template <bool PHILOX>
 __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_constant__ StepParams P) {
   __shared__ double s_wmax[kWarps];
   __shared__ int s_last;
+  __shared__ StepShared sh;
+  stage_hyper(P, sh);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const eco_i8eco_hyper_t& H = P.H;
+  const eco_i8eco_hyper_t& H = sh.H;
   for (i64 t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
     int li = 0;
     while (li + 1 < P.n_layers && P.layers[li + 1].tile_begin <= t) ++li;
@@ -365,13 +396,13 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
         const bool hm = c.com_m >= 32, hg = c.com_g >= 32;
         int rmx;
         if (!hm && !hg)
-          rmx = fast32_row<false, false>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+          rmx = fast32_row<false, false>(c, sh.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
         else if (hm && !hg)
-          rmx = fast32_row<true, false>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+          rmx = fast32_row<true, false>(c, sh.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
         else if (!hm && hg)
-          rmx = fast32_row<false, true>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+          rmx = fast32_row<false, true>(c, sh.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
         else
-          rmx = fast32_row<true, true>(c, P.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
+          rmx = fast32_row<true, true>(c, sh.keys, H.seed, L.stream_w, row, wr, mr, gr, (int)(L.cols / 16), lane, rsum);
         rmax = rmx;
       } else if (c.fast) {
         FastRow fr;
@@ -391,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
           int rsum32 = 0;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const Philox4 rnd = sr_quad_k(P.keys, L.stream_w, row, (uint32_t)((c0 >> 2) + q));
+            const Philox4 rnd = sr_quad_k(sh.keys, L.stream_w, row, (uint32_t)((c0 >> 2) + q));
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int e = 4 * q + k;
@@ -413,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 2) i8eco_step_kernel(const __grid_co
         // exact int64 path: any shape, any alignment, replay mode, wide intermediates
         for (i64 c0 = 4 * lane; c0 < L.cols; c0 += 128) {
           Philox4 rnd{0u, 0u, 0u, 0u};
-          if (PHILOX) rnd = sr_quad_k(P.keys, L.stream_w, row, (uint32_t)(c0 >> 2));
+          if (PHILOX) rnd = sr_quad_k(sh.keys, L.stream_w, row, (uint32_t)(c0 >> 2));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const i64 col = c0 + k;

@@ -187,11 +187,11 @@ ECO_DEV void epi_store_s32(const GemmParams& p, const uint32_t (&v)[32], int m, 
 
 // Fused requant epilogue for one 32-column chunk of one row: one Philox call per
 // four columns (the element's 32-bit field; exact tie-break draws only when needed).
-ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int m, int nb, int bias_lane,
-                               int mult_lane) {
+ECO_DEV void epi_store_requant(const GemmParams& p, const eco_sr_t& sr, const PhiloxKeys& keys,
+                               const uint32_t (&v)[32], int m, int nb, int bias_lane, int mult_lane) {
   uint32_t packed[8];
-  const uint32_t row = (uint32_t)(p.sr.row_base + m);
-  const bool philox = p.sr.mode == ECO_SR_PHILOX && p.shift >= 0;
+  const uint32_t row = (uint32_t)(sr.row_base + m);
+  const bool philox = sr.mode == ECO_SR_PHILOX && p.shift >= 0;
   if (philox && p.shift > 32 && p.shift <= 62) {
     // The usual forward case: single-instruction wide products, the 32-bit Philox field
     // added in place by a multiply-add, the 2^-32 tie test out of the per-element branch
@@ -201,7 +201,7 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
     const int lower = p.relu ? 0 : -127;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const Philox4 rnd = sr_quad_k(p.keys, p.sr.stream, row, (uint32_t)((nb >> 2) + q));
+      const Philox4 rnd = sr_quad_k(keys, sr.stream, row, (uint32_t)((nb >> 2) + q));
       int y4[4];
       unsigned ties = 0u;
 #pragma unroll
@@ -220,8 +220,8 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
           const int x = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
           const i64 prod = mul_wide_s32(x, __shfl_sync(0xffffffffu, mult_lane, e));
           if ((ties >> k) & 1u)
-            y4[k] = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, quad_word(rnd, k), p.sr.seed,
-                                                               p.sr.stream, row, (uint32_t)(nb + e))));
+            y4[k] = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, quad_word(rnd, k), sr.seed,
+                                                               sr.stream, row, (uint32_t)(nb + e))));
         }
       }
       packed[q] = pack4(max(min(y4[0], 127), lower), max(min(y4[1], 127), lower), max(min(y4[2], 127), lower),
@@ -231,7 +231,7 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     Philox4 rnd{0u, 0u, 0u, 0u};
-    if (philox) rnd = sr_quad_k(p.keys, p.sr.stream, row, (uint32_t)((nb >> 2) + q));
+    if (philox) rnd = sr_quad_k(keys, sr.stream, row, (uint32_t)((nb >> 2) + q));
     packed[q] = 0u;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -242,15 +242,15 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const uint32_t (&v)[32], int
       if (p.shift < 0) {
         yv = shl64(prod, -p.shift);
       } else if (philox) {
-        yv = sr_round(prod, p.shift, quad_word(rnd, k), p.sr.seed, p.sr.stream, row, (uint32_t)(nb + e));
-      } else if (p.sr.mode == ECO_SR_NEAREST) {
+        yv = sr_round(prod, p.shift, quad_word(rnd, k), sr.seed, sr.stream, row, (uint32_t)(nb + e));
+      } else if (sr.mode == ECO_SR_NEAREST) {
         yv = sar64(add64(prod, half_nudge(p.shift)), p.shift);
       } else {
         i64 nud = 0;
         if (m < p.M && nb + e < p.N) {
-          const i64 idx = (i64)m * p.sr.nudge_ld + nb + e;
-          nud = p.sr.mode == ECO_SR_REPLAY32 ? (i64) static_cast<const int32_t*>(p.sr.nudge)[idx]
-                                            : static_cast<const i64*>(p.sr.nudge)[idx];
+          const i64 idx = (i64)m * sr.nudge_ld + nb + e;
+          nud = sr.mode == ECO_SR_REPLAY32 ? (i64) static_cast<const int32_t*>(sr.nudge)[idx]
+                                            : static_cast<const i64*>(sr.nudge)[idx];
         }
         yv = sar64(add64(prod, nud), p.shift);
       }
@@ -395,6 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kChunks = BN / 64;  // 32-column chunks per half
     i64 amax = 0;
     int j = 0;
+    PhiloxKeys keys;
+    const eco_sr_t sr = sr_resolve(p.sr, p.keys, keys);
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
       const int b = j & 1;
       if (!mbar_wait(&tfull[b], (uint32_t)(j >> 1) & 1u) || *abort_flag) {
@@ -418,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_store_s32(p, v, m, nb, bias_lane, amax);
         } else {
           const int mult_lane = n_lane < p.N ? __ldg(p.mult + n_lane) : 0;
-          epi_store_requant(p, v, m, nb, bias_lane, mult_lane);
+          epi_store_requant(p, sr, keys, v, m, nb, bias_lane, mult_lane);
         }
       }
       tc_fence_before();
@@ -546,7 +548,7 @@ extern "C" int eco_gemm_s8_requant(const int8_t* A, int64_t lda, int a_layout, c
   p.shift = shift;
   p.relu = relu;
   p.sr = sr;
-  p.keys = philox_keys(sr.seed);
+  p.keys = philox_keys(sr.mode == ECO_SR_PHILOX ? sr.seed : 0);
   p.Y = Y;
   p.ldy = ldy;
   return gemm_common(A, lda, a_layout, B, ldb, b_layout, M, N, K, p, 1, eco_stream(stream), "eco_gemm_s8_requant");

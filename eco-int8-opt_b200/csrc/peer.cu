@@ -30,6 +30,7 @@ struct PushArgs {
   int64_t* flags[ECO_MAX_PEERS];
   int n_ranks, rank, slot;
   int64_t epoch;
+  const int64_t* epoch_dev;  // nullable: the epoch, read when the kernel runs
   unsigned* ticket;  // zero between launches; the last CTA resets it
 };
 
@@ -82,8 +83,9 @@ __global__ void __launch_bounds__(kPushThreads) peer_push_kernel(const __grid_co
     if (threadIdx.x == 0 && atomicAdd(A.ticket, 1u) == gridDim.x - 1) {  // every CTA has fenced
       *A.ticket = 0u;
       asm volatile("fence.sc.sys;" ::: "memory");
+      const int64_t epoch = A.epoch_dev ? *A.epoch_dev : A.epoch;
       for (int p = 0; p < A.n_ranks; ++p)
-        st_release_sys(A.flags[p] + (int64_t)A.slot * ECO_MAX_PEERS + A.rank, A.epoch);
+        st_release_sys(A.flags[p] + (int64_t)A.slot * ECO_MAX_PEERS + A.rank, epoch);
     }
   }
 }
@@ -104,17 +106,21 @@ ECO_DEV unsigned long long peer_clock() {
 
 // Thread p publishes `epoch` in slot (slot, rank) of rank p's flag array, after
 // everything this stream did before (the previous kernels' stores included).
-__global__ void peer_signal_kernel(const __grid_constant__ FlagArgs F, int n, int rank, int slot, int64_t epoch) {
+__global__ void peer_signal_kernel(const __grid_constant__ FlagArgs F, int n, int rank, int slot, int64_t epoch,
+                                   const int64_t* epoch_dev) {
   const int p = threadIdx.x;
   if (p >= n) return;
+  if (epoch_dev) epoch = *epoch_dev;
   asm volatile("fence.sc.sys;" ::: "memory");
   st_release_sys(F.peer_flags[p] + (int64_t)slot * ECO_MAX_PEERS + rank, epoch);
 }
 
 // Thread p waits until rank p's entry of `slot` in this rank's flags reaches `epoch`.
-__global__ void peer_wait_kernel(const int64_t* flags, int n, int slot, int64_t epoch, unsigned long long limit_ns) {
+__global__ void peer_wait_kernel(const int64_t* flags, int n, int slot, int64_t epoch, const int64_t* epoch_dev,
+                                 unsigned long long limit_ns) {
   const int p = threadIdx.x;
   if (p >= n) return;
+  if (epoch_dev) epoch = *epoch_dev;
   const int64_t* f = flags + (int64_t)slot * ECO_MAX_PEERS + p;
   if (ld_acquire_sys(f) >= epoch) return;
   const unsigned long long t0 = peer_clock();
@@ -137,6 +143,7 @@ struct AllreduceArgs {
   const void* src;
   int src_bits, count, stride, op, n, rank, slot;
   int64_t epoch;
+  const int64_t* epoch_dev;  // nullable: the epoch, read when the kernel runs
   int64_t* bufs[ECO_MAX_PEERS];
   int64_t* flags[ECO_MAX_PEERS];
   const int64_t* own_buf;
@@ -152,7 +159,8 @@ ECO_DEV int64_t ld_relaxed_sys(const int64_t* p) {
 }
 
 __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_constant__ AllreduceArgs A) {
-  const int par = (int)(A.epoch & 1);
+  const int64_t epoch = A.epoch_dev ? *A.epoch_dev : A.epoch;
+  const int par = (int)(epoch & 1);
   for (int e = threadIdx.x; e < A.count; e += blockDim.x) {
     const int64_t v = A.src_bits == 32 ? (int64_t) static_cast<const int32_t*>(A.src)[e]
                                        : static_cast<const int64_t*>(A.src)[e];
@@ -162,16 +170,16 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const __grid_consta
   __syncthreads();
   if (threadIdx.x < A.n) {
     asm volatile("fence.sc.sys;" ::: "memory");
-    st_release_sys(A.flags[threadIdx.x] + (int64_t)A.slot * ECO_MAX_PEERS + A.rank, A.epoch);
+    st_release_sys(A.flags[threadIdx.x] + (int64_t)A.slot * ECO_MAX_PEERS + A.rank, epoch);
   }
   __shared__ int s_late;
   if (threadIdx.x == 0) s_late = 0;
   __syncthreads();
   if (threadIdx.x < A.n) {
     const int64_t* f = A.own_flags + (int64_t)A.slot * ECO_MAX_PEERS + threadIdx.x;
-    if (ld_acquire_sys(f) < A.epoch) {
+    if (ld_acquire_sys(f) < epoch) {
       const unsigned long long t0 = peer_clock();
-      while (ld_acquire_sys(f) < A.epoch) {
+      while (ld_acquire_sys(f) < epoch) {
         if (peer_clock() - t0 > A.limit_ns) {
           atomicOr(&g_peer_errors, ECO_FLAG_WAIT_TIMEOUT);
           s_late = 1;
@@ -205,7 +213,8 @@ int eco_peer_errors_take(unsigned* out) {
 
 static int peer_push(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols, int8_t* const* dst, int n_dst,
                      int64_t ld_dst, int64_t dst_row0, int split, int ctas, int64_t* const* peer_flags, int n_ranks,
-                     int rank, int slot, int64_t epoch, unsigned* ticket, eco_stream_t stream) {
+                     int rank, int slot, int64_t epoch, const int64_t* epoch_dev, unsigned* ticket,
+                     eco_stream_t stream) {
   ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && ld_src >= cols && dst_row0 >= 0, ECO_ERR_ARG,
               "eco_peer_push_s8: bad arguments");
   ECO_REQUIRE(n_dst >= 1 && n_dst <= ECO_MAX_PEERS, ECO_ERR_ARG, "eco_peer_push_s8: 1..%d destinations",
@@ -236,7 +245,7 @@ static int peer_push(const int8_t* src, int64_t ld_src, int64_t rows, int64_t co
   A.ticket = ticket;
   if (ticket) {
     ECO_REQUIRE(peer_flags && n_ranks >= 1 && n_ranks <= ECO_MAX_PEERS && rank >= 0 && rank < n_ranks &&
-                    slot >= 0 && epoch > 0,
+                    slot >= 0 && (epoch > 0 || epoch_dev),
                 ECO_ERR_ARG, "eco_peer_push_signal_s8: bad signal arguments");
     for (int p = 0; p < n_ranks; ++p) {
       ECO_REQUIRE(peer_flags[p], ECO_ERR_ARG, "eco_peer_push_signal_s8: null flag array %d", p);
@@ -246,6 +255,7 @@ static int peer_push(const int8_t* src, int64_t ld_src, int64_t rows, int64_t co
     A.rank = rank;
     A.slot = slot;
     A.epoch = epoch;
+    A.epoch_dev = epoch_dev;
   }
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(rows, ctas > 0 ? ctas : eco_num_sms()));
   if (vec)
@@ -259,49 +269,52 @@ extern "C" int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows,
                                 int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas,
                                 eco_stream_t stream) {
   return peer_push(src, ld_src, rows, cols, dst, n_dst, ld_dst, dst_row0, split, ctas, nullptr, 0, 0, 0, 0, nullptr,
-                   stream);
+                   nullptr, stream);
 }
 
 extern "C" int eco_peer_push_signal_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols,
                                        int8_t* const* dst, int n_dst, int64_t ld_dst, int64_t dst_row0, int split,
                                        int ctas, int64_t* const* peer_flags, int n_ranks, int rank, int slot,
-                                       int64_t epoch, uint32_t* ticket, eco_stream_t stream) {
+                                       int64_t epoch, const int64_t* epoch_dev, uint32_t* ticket,
+                                       eco_stream_t stream) {
   ECO_REQUIRE(ticket, ECO_ERR_ARG, "eco_peer_push_signal_s8: ticket word required");
   return peer_push(src, ld_src, rows, cols, dst, n_dst, ld_dst, dst_row0, split, ctas, peer_flags, n_ranks, rank,
-                   slot, epoch, ticket, stream);
+                   slot, epoch, epoch_dev, ticket, stream);
 }
 
 extern "C" int eco_peer_signal(int64_t* const* peer_flags, int n, int rank, int slot, int64_t epoch,
-                               eco_stream_t stream) {
-  ECO_REQUIRE(peer_flags && n >= 1 && n <= ECO_MAX_PEERS && rank >= 0 && rank < n && slot >= 0 && epoch > 0,
+                               const int64_t* epoch_dev, eco_stream_t stream) {
+  ECO_REQUIRE(peer_flags && n >= 1 && n <= ECO_MAX_PEERS && rank >= 0 && rank < n && slot >= 0 &&
+                  (epoch > 0 || epoch_dev),
               ECO_ERR_ARG, "eco_peer_signal: bad arguments");
   FlagArgs F;
   for (int p = 0; p < ECO_MAX_PEERS; ++p) {
     F.peer_flags[p] = p < n ? peer_flags[p] : nullptr;
     if (p < n) ECO_REQUIRE(peer_flags[p], ECO_ERR_ARG, "eco_peer_signal: null flag array %d", p);
   }
-  peer_signal_kernel<<<1, 32, 0, eco_stream(stream)>>>(F, n, rank, slot, epoch);
+  peer_signal_kernel<<<1, 32, 0, eco_stream(stream)>>>(F, n, rank, slot, epoch, epoch_dev);
   return eco_launch_check("eco_peer_signal");
 }
 
-extern "C" int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, int64_t timeout_us,
-                             eco_stream_t stream) {
-  ECO_REQUIRE(flags && n >= 1 && n <= ECO_MAX_PEERS && slot >= 0 && epoch > 0 && timeout_us >= 0, ECO_ERR_ARG,
+extern "C" int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, const int64_t* epoch_dev,
+                             int64_t timeout_us, eco_stream_t stream) {
+  ECO_REQUIRE(flags && n >= 1 && n <= ECO_MAX_PEERS && slot >= 0 && (epoch > 0 || epoch_dev) && timeout_us >= 0,
+              ECO_ERR_ARG,
               "eco_peer_wait: bad arguments");
   const unsigned long long limit = timeout_us > 0 ? std::min<unsigned long long>((unsigned long long)timeout_us * 1000ull,
                                                                                 kPeerWaitNs)
                                                   : kPeerWaitNs;
-  peer_wait_kernel<<<1, 32, 0, eco_stream(stream)>>>(flags, n, slot, epoch, limit);
+  peer_wait_kernel<<<1, 32, 0, eco_stream(stream)>>>(flags, n, slot, epoch, epoch_dev, limit);
   return eco_launch_check("eco_peer_wait");
 }
 
 extern "C" int eco_peer_allreduce_i64(const void* src, int src_bits, int count, int op, int64_t* const* bufs,
                                       int stride, const int64_t* own_buf, int64_t* const* peer_flags,
                                       const int64_t* own_flags, int n, int rank, int slot, int64_t epoch,
-                                      int64_t* out, eco_stream_t stream) {
+                                      const int64_t* epoch_dev, int64_t* out, eco_stream_t stream) {
   ECO_REQUIRE(src && bufs && own_buf && peer_flags && own_flags && out && (src_bits == 32 || src_bits == 64) &&
                   count >= 1 && stride >= count && (op == 0 || op == 1) && n >= 1 && n <= ECO_MAX_PEERS &&
-                  rank >= 0 && rank < n && slot >= 0 && epoch > 0,
+                  rank >= 0 && rank < n && slot >= 0 && (epoch > 0 || epoch_dev),
               ECO_ERR_ARG, "eco_peer_allreduce_i64: bad arguments");
   AllreduceArgs A{};
   A.src = src;
@@ -313,6 +326,7 @@ extern "C" int eco_peer_allreduce_i64(const void* src, int src_bits, int count, 
   A.rank = rank;
   A.slot = slot;
   A.epoch = epoch;
+  A.epoch_dev = epoch_dev;
   for (int p = 0; p < n; ++p) {
     ECO_REQUIRE(bufs[p] && peer_flags[p], ECO_ERR_ARG, "eco_peer_allreduce_i64: null buffer %d", p);
     A.bufs[p] = bufs[p];

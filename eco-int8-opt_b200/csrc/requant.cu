@@ -81,6 +81,8 @@ struct RequantArgs {
 // columns of a row per iteration (one 64-byte load of int32, one 16-byte store).
 template <bool VEC, int MODE>
 __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) {
+  PhiloxKeys keys;
+  const eco_sr_t sr = sr_resolve(a.sr, a.keys, keys);
   const i64 cpr = (a.cols + 15) / 16;
   const i64 total = a.rows * cpr;
   const int shift = a.dparams ? (int)a.dparams[2] : a.shift;
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
     for (int q = 0; q < 4; ++q) {
       Philox4 rnd{0u, 0u, 0u, 0u};
       if (MODE == 1 && !left && !zero_out)
-        rnd = sr_quad_k(a.keys, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)((c0 >> 2) + q));
+        rnd = sr_quad_k(keys, sr.stream, (uint32_t)(sr.row_base + r), (uint32_t)((c0 >> 2) + q));
       packed[q] = 0u;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -128,10 +130,10 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
         else if (MODE == 0)
           yv = sar64(add64(prod, half_nudge(shift)), shift);
         else if (MODE == 1)
-          yv = sr_round(prod, shift, quad_word(rnd, k), a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r),
+          yv = sr_round(prod, shift, quad_word(rnd, k), sr.seed, sr.stream, (uint32_t)(sr.row_base + r),
                         (uint32_t)c);
         else
-          yv = in ? sar64(add64(prod, replay_nudge(a.sr, r, c)), shift) : 0;
+          yv = in ? sar64(add64(prod, replay_nudge(sr, r, c)), shift) : 0;
         int8_t y = sat8(yv);
         if (a.relu && y < 0) y = 0;
         if (a.mask && in && a.mask[r * a.ld_mask + c] <= 0) y = 0;
@@ -158,12 +160,10 @@ __global__ void __launch_bounds__(kThreads) requant_kernel(const RequantArgs a) 
 // four Philox calls.  0 <= shift <= 62, and with |x * mult| < 2^62 every result of
 // a shift > 32 fits int32, so the tail arithmetic is 32-bit.
 template <bool MASK, bool SUMSQ, bool COLM, bool BIAS, bool BIG>
-__global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantArgs a) {
+ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
+  PhiloxKeys keys;
+  const eco_sr_t sr = sr_resolve(a.sr, a.keys, keys);
   const int cpr = (int)(a.cols >> 4);
-  const int sh = a.dparams ? (int)a.dparams[2] : a.shift;
-  // with device parameters both variants are launched and the one that does not
-  // match the shift returns; a shift beyond 62 or below 0 is the small variant's
-  if (a.dparams && BIG != (sh > 32 && sh <= 62)) return;
   const bool zero_out = sh > 62;
   const int lo = sh - 32;  // BIG: bits of the tie-break draw
   const uint32_t pow2lo = BIG ? 1u << lo : 0u;
@@ -204,14 +204,14 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
       for (int q = 0; q < 4; ++q) nx[q] = reinterpret_cast<const int4*>(a.src + r * a.ld_src + j * 16)[q];
       if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + j * 16);
     }
-    const uint32_t grow = (uint32_t)(a.sr.row_base + cr);
+    const uint32_t grow = (uint32_t)(sr.row_base + cr);
     const int8_t* mb = reinterpret_cast<const int8_t*>(&mk);
     const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mk);
     uint32_t packed[4];
     int sq32 = 0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const Philox4 rnd = sr_quad_k(a.keys, a.sr.stream, grow, (uint32_t)((c0 >> 2) + q));
+      const Philox4 rnd = sr_quad_k(keys, sr.stream, grow, (uint32_t)((c0 >> 2) + q));
       int y4[4];
       unsigned ties = 0u;
 #pragma unroll
@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
           int x = v[4 * q + k];
           if (BIAS) x = add32(x, a.bias[c]);
           const i64 prod = mul_wide_s32(x, COLM ? a.mult_col[c] : mult_s);
-          y4[k] = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, quad_word(rnd, k), a.sr.seed, a.sr.stream,
+          y4[k] = (int)max((i64)-128, min((i64)128, sr_round(prod, sh, quad_word(rnd, k), sr.seed, sr.stream,
                                                              grow, (uint32_t)c)));
         }
       }
@@ -268,6 +268,23 @@ __global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantA
   if (SUMSQ) block_reduce_to<false>(sq, a.sumsq);
 }
 
+template <bool MASK, bool SUMSQ, bool COLM, bool BIAS, bool BIG>
+__global__ void __launch_bounds__(kThreads) requant_philox_kernel(const RequantArgs a) {
+  requant_philox_body<MASK, SUMSQ, COLM, BIAS, BIG>(a, a.shift);
+}
+
+// The requant whose multiplier and shift the device computed (eco_scale_from_amax):
+// one launch that takes the wide (shift 33..62) or the narrow path by the shift it
+// reads; a shift beyond 62 or below 0 is the narrow path's.
+template <bool MASK, bool SUMSQ>
+__global__ void __launch_bounds__(kThreads) requant_philox_dev_kernel(const RequantArgs a) {
+  const int sh = (int)a.dparams[2];
+  if (sh > 32 && sh <= 62)
+    requant_philox_body<MASK, SUMSQ, false, false, true>(a, sh);
+  else
+    requant_philox_body<MASK, SUMSQ, false, false, false>(a, sh);
+}
+
 struct AmsArgs {
   const void* x;
   int x_bits;
@@ -281,6 +298,7 @@ struct AmsArgs {
 };
 
 __global__ void __launch_bounds__(kThreads) ams_kernel(const AmsArgs a) {
+  const eco_sr_t sr = sr_resolve(a.sr);
   const i64 n = a.rows * a.cols;
   for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (i64)gridDim.x * blockDim.x) {
     const i64 r = i / a.cols, c = i - r * a.cols;
@@ -288,10 +306,10 @@ __global__ void __launch_bounds__(kThreads) ams_kernel(const AmsArgs a) {
             : a.x_bits == 32 ? (i64)static_cast<const int32_t*>(a.x)[i]
                              : static_cast<const i64*>(a.x)[i];
     const i64 m = a.mult_kind == 0 ? a.mult_scalar : (a.mult_kind == 1 ? a.mult[c] : a.mult[r]);
-    const uint32_t f = (a.sr.mode == ECO_SR_PHILOX && a.shift >= 0)
-                           ? sr_field(a.sr.seed, a.sr.stream, (uint32_t)(a.sr.row_base + r), (uint32_t)c)
+    const uint32_t f = (sr.mode == ECO_SR_PHILOX && a.shift >= 0)
+                           ? sr_field(sr.seed, sr.stream, (uint32_t)(sr.row_base + r), (uint32_t)c)
                            : 0u;
-    a.out[i] = round_elem(a.sr, a.shift, mul64(x, m), r, c, f);
+    a.out[i] = round_elem(sr, a.shift, mul64(x, m), r, c, f);
   }
 }
 
@@ -353,23 +371,21 @@ extern "C" int eco_requant_s32_s8_dev(const int32_t* src, int64_t rows, int64_t 
   ECO_REQUIRE(src && dst && params && rows >= 0 && cols >= 0 && ld_src >= cols && ld_dst >= cols, ECO_ERR_ARG,
               "eco_requant_s32_s8_dev: bad arguments");
   ECO_REQUIRE(!mask || ld_mask >= cols, ECO_ERR_ARG, "eco_requant_s32_s8_dev: bad mask leading dim");
-  ECO_REQUIRE(sr.mode == ECO_SR_PHILOX, ECO_ERR_ARG, "eco_requant_s32_s8_dev: Philox rounding only");
+  ECO_REQUIRE(sr.mode == ECO_SR_PHILOX || sr.mode == ECO_SR_PHILOX_DEV, ECO_ERR_ARG,
+              "eco_requant_s32_s8_dev: Philox rounding only");
+  if (int rc = eco_check_sr(sr, 0, "eco_requant_s32_s8_dev")) return rc;
   cudaStream_t s = eco_stream(stream);
   if (sumsq && cudaMemsetAsync(sumsq, 0, sizeof(int64_t), s) != cudaSuccess)
     return eco_launch_check("eco_requant_s32_s8_dev memset");
   if (rows == 0 || cols == 0) return ECO_OK;
   RequantArgs a{src, rows, cols, ld_src, nullptr, nullptr, 0, 0, relu, sr,
-                mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq), 1, philox_keys(sr.seed),
-                reinterpret_cast<const i64*>(params)};
+                mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq), 1,
+                philox_keys(sr.mode == ECO_SR_PHILOX ? sr.seed : 0), reinterpret_cast<const i64*>(params)};
   const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
                    ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0));
   if (vec) {
     const int gp = (int)std::max<i64>(1, std::min<i64>(rows, (i64)eco_num_sms() * 8));
-#define ECO_RQD(M, Q)                                                                   \
-  do {                                                                                  \
-    requant_philox_kernel<M, Q, false, false, true><<<gp, kThreads, 0, s>>>(a);         \
-    requant_philox_kernel<M, Q, false, false, false><<<gp, kThreads, 0, s>>>(a);        \
-  } while (0)
+#define ECO_RQD(M, Q) requant_philox_dev_kernel<M, Q><<<gp, kThreads, 0, s>>>(a)
     if (mask) {
       if (sumsq) ECO_RQD(true, true); else ECO_RQD(true, false);
     } else {
@@ -397,14 +413,16 @@ extern "C" int eco_requant_s32_s8(const int32_t* src, int64_t rows, int64_t cols
   if (rows == 0 || cols == 0) return ECO_OK;
   RequantArgs a{src, rows, cols, ld_src, bias_col, mult_col, mult_scalar, shift, relu, sr,
                 mask, ld_mask, dst, ld_dst, reinterpret_cast<i64*>(sumsq),
-                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX, philox_keys(sr.seed), nullptr};
+                mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX,
+                philox_keys(sr.mode == ECO_SR_PHILOX ? sr.seed : 0), nullptr};
   const bool replay = sr.mode == ECO_SR_REPLAY32 || sr.mode == ECO_SR_REPLAY64;
   const bool vec = cols % 16 == 0 && eco_aligned16(src) && ld_src % 4 == 0 && eco_aligned16(dst) &&
                    ld_dst % 16 == 0 && (!mask || (eco_aligned16(mask) && ld_mask % 16 == 0)) &&
                    (!bias_col || eco_aligned16(bias_col)) && (!mult_col || eco_aligned16(mult_col));
   (void)replay;
   const i64 work = rows * ((cols + 15) / 16);
-  const int mode = sr.mode == ECO_SR_NEAREST ? 0 : (sr.mode == ECO_SR_PHILOX ? 1 : 2);
+  const int mode =
+      sr.mode == ECO_SR_NEAREST ? 0 : ((sr.mode == ECO_SR_PHILOX || sr.mode == ECO_SR_PHILOX_DEV) ? 1 : 2);
   const bool mult_ok = mult_col || (mult_scalar >= INT32_MIN && mult_scalar <= INT32_MAX);
   if (vec && mode == 1 && shift >= 0 && mult_ok) {
     const int gp = (int)std::max<i64>(1, std::min<i64>(rows, (i64)eco_num_sms() * 8));

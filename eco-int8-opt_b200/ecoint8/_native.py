@@ -17,7 +17,7 @@ _PKG_ROOT = pathlib.Path(__file__).resolve().parent.parent
 LIB_PATH = _PKG_ROOT / "lib" / "libecoint8_b200.so"
 
 ECO_OK = 0
-SR_NEAREST, SR_PHILOX, SR_REPLAY32, SR_REPLAY64, SR_REPLAY_F32 = 0, 1, 2, 3, 4
+SR_NEAREST, SR_PHILOX, SR_REPLAY32, SR_REPLAY64, SR_REPLAY_F32, SR_PHILOX_DEV = 0, 1, 2, 3, 4, 5
 FLAG_SHIFT_OVERFLOW, FLAG_BAD_RATIO, FLAG_WAIT_TIMEOUT = 1, 2, 4
 
 c_i64, c_u64, c_i32, c_u32, c_p, c_d, c_f = (ctypes.c_int64, ctypes.c_uint64, ctypes.c_int32, ctypes.c_uint32,
@@ -46,7 +46,8 @@ class I8ECOHyper(ctypes.Structure):
     """``eco_i8eco_hyper_t``."""
 
     _fields_ = [("lr", c_d), ("grad_clip", c_d), ("b_q", c_i64), ("nb_q", c_i64), ("lr_q", c_i64),
-                ("a_q", c_i64), ("sr_mode", c_i32), ("finalize", c_i32), ("seed", c_u64), ("done_counter", c_p)]
+                ("a_q", c_i64), ("sr_mode", c_i32), ("finalize", c_i32), ("seed", c_u64), ("done_counter", c_p),
+                ("dev", c_p)]
 
 
 # name -> (restype, argtypes); one line per entry point of the header
@@ -65,11 +66,11 @@ _SIGS = {
                                        c_p]),
     "eco_peer_push_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, c_i64, c_i64, c_i32, c_i32, c_p]),
     "eco_peer_push_signal_s8": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_i32, c_i64, c_i64, c_i32, c_i32, c_p, c_i32,
-                                        c_i32, c_i32, c_i64, c_p, c_p]),
+                                        c_i32, c_i32, c_i64, c_p, c_p, c_p]),
     "eco_peer_allreduce_i64": (c_i32, [c_p, c_i32, c_i32, c_i32, c_p, c_i32, c_p, c_p, c_p, c_i32, c_i32, c_i32, c_i64,
-                                       c_p, c_p]),
-    "eco_peer_signal": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i64, c_p]),
-    "eco_peer_wait": (c_i32, [c_p, c_i32, c_i32, c_i64, c_i64, c_p]),
+                                       c_p, c_p, c_p]),
+    "eco_peer_signal": (c_i32, [c_p, c_i32, c_i32, c_i32, c_i64, c_p, c_p]),
+    "eco_peer_wait": (c_i32, [c_p, c_i32, c_i32, c_i64, c_p, c_i64, c_p]),
     "eco_ce_grad_rowstats": (c_i32, [c_p, c_i64, c_i64, c_i64, c_d, c_p, c_i64, c_p, c_p, c_p, c_p]),
     "eco_ce_grad_quantize": (c_i32, [c_p, c_i64, c_i64, c_i64, c_d, c_p, c_i64, c_p, c_p, c_i32, SRSpec, c_p, c_i64,
                                      c_p, c_p, c_p, c_p, c_p]),
@@ -168,7 +169,20 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 def sr_spec(mode=SR_NEAREST, nudge: torch.Tensor | None = None, seed=0, stream_id=0, row_base=0) -> SRSpec:
+    """``eco_sr_t``.  A ``seed`` that is a device key (``_graphs.DevKey``, a word of a
+    captured graph's table) turns a Philox site into ``ECO_SR_PHILOX_DEV``."""
     s = SRSpec()
+    dev_key = getattr(seed, "ptr", None)
+    if dev_key is not None:
+        if mode != SR_PHILOX:
+            raise ValueError("a device key needs a Philox site")
+        s.mode = SR_PHILOX_DEV
+        s.nudge = dev_key
+        s.nudge_ld = 0
+        s.seed = 0
+        s.stream = stream_id & 0xFFFFFFFFFFFFFFFF
+        s.row_base = row_base
+        return s
     s.mode = mode
     s.nudge = ptr(nudge)
     s.nudge_ld = 0 if nudge is None else (nudge.shape[-1] if nudge.dim() else 1)

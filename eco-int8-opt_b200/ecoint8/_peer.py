@@ -35,8 +35,10 @@ import torch.distributed as dist
 from . import _native as nat
 
 MAX_PEERS = 8  # ECO_MAX_PEERS of the C ABI
-MAX_SLOTS = 3 * 256 + 1  # three flag slots per row-sharded layer, one for the small all-reduces
-RED_SLOT = MAX_SLOTS - 1
+MAX_LAYERS = 256  # row-sharded layers per exchange
+MAX_SLOTS = 4 * MAX_LAYERS + 2  # four flag slots per layer, the small all-reduces', the row sums'
+RED_SLOT = MAX_SLOTS - 2
+ROWSUM_SLOT = MAX_SLOTS - 1
 RED_STRIDE = 1024  # longest vector of the small all-reduce
 HANDLE_BYTES = 64  # ECO_IPC_HANDLE_BYTES of the C ABI
 
@@ -85,9 +87,9 @@ class Shared:
 class LayerBufs:
     def __init__(self, ex: "Exchange", layer, b: int):
         idx = len(ex.layers)
-        if 3 * idx + 3 > RED_SLOT:
+        if idx >= MAX_LAYERS:
             raise RuntimeError("ecoint8.parallel: too many row-sharded layers for the peer exchange")
-        self.slot_x, self.slot_dy, self.slot_w = 3 * idx, 3 * idx + 1, 3 * idx + 2
+        self.slot_x, self.slot_dy, self.slot_w, self.slot_gb = 4 * idx, 4 * idx + 1, 4 * idx + 2, 4 * idx + 3
         n, dev, g = ex.n, ex.dev, ex.group
         out, in_f = layer.w_i8.shape
         self.b, self.out, self.in_f = b, out, in_f
@@ -96,10 +98,15 @@ class LayerBufs:
         self.w = Shared((out, in_f), torch.int8, dev, g, ex.maps)
         self.w.t.copy_(layer.w_i8)
         layer._buffers["w_i8"] = self.w.t  # the weights live in the shared buffer from now on
+        # the bias gradient's column sums over the global batch: each rank forms its rows
+        # and stores them into every rank's copy
+        self.gb = Shared((out,), torch.int64, dev, g, ex.maps)
         self.layer = weakref.ref(layer)
         self.x_ptrs = _arr(self.x.ptrs)
         self.dy_ptrs = _arr(self.dy.ptrs)
         self.w_peers = _arr([p for r, p in enumerate(self.w.ptrs) if r != ex.rank])
+        lo = ex.rank * out // n
+        self.gb_peers = _arr([p + 8 * lo for r, p in enumerate(self.gb.ptrs) if r != ex.rank])
         self.done = torch.cuda.Event()  # the layer's dW rows are formed (recorded on the dW stream)
 
 
@@ -128,15 +135,43 @@ class Exchange:
         self.red = Shared((2, self.n, RED_STRIDE), torch.int64, device, group, self.maps)  # small all-reduce areas
         self.red_ptrs = _arr(self.red.ptrs)
         self.layers: dict[int, LayerBufs] = {}
+        self.rowsum: Shared | None = None  # the optimizer's per-row |e| sums, [world, rows] (one row per rank)
+
+    # -- epochs -------------------------------------------------------------------
+    # Every signal on a slot advances the slot's epoch; a wait waits for the current one.
+    # While a StepGraph is captured the host epochs do not move: each call takes a word
+    # of the graph's table, and every replay advances the epochs in the same order.
+    def _next_epoch(self, slot: int):
+        """(host epoch, device word or None) of a signal on ``slot``."""
+        from . import graphs
+
+        g = graphs.capturing()
+        if g is not None:
+            def bump(slot=slot):
+                self.epoch[slot] += 1
+                return self.epoch[slot]
+
+            return 0, g.table.word(bump)
+        self.epoch[slot] += 1
+        return self.epoch[slot], None
+
+    def _current_epoch(self, slot: int):
+        from . import graphs
+
+        g = graphs.capturing()
+        if g is not None:
+            return 0, g.table.word(lambda slot=slot: self.epoch[slot])
+        return self.epoch[slot], None
 
     # -- flags ------------------------------------------------------------------
     def signal(self, slot: int, stream) -> None:
-        self.epoch[slot] += 1
-        nat.call("eco_peer_signal", self.flag_ptrs, self.n, self.rank, slot, self.epoch[slot], stream.cuda_stream)
+        e, e_dev = self._next_epoch(slot)
+        nat.call("eco_peer_signal", self.flag_ptrs, self.n, self.rank, slot, e, e_dev, stream.cuda_stream)
 
     def wait(self, slot: int, stream) -> None:
         if self.epoch[slot] > 0:
-            nat.call("eco_peer_wait", self.flags.t.data_ptr(), self.n, slot, self.epoch[slot], 0, stream.cuda_stream)
+            e, e_dev = self._current_epoch(slot)
+            nat.call("eco_peer_wait", self.flags.t.data_ptr(), self.n, slot, e, e_dev, 0, stream.cuda_stream)
 
     def allreduce(self, src: torch.Tensor, op: str) -> torch.Tensor:
         """MAX or SUM over the ranks of a short int32/int64 vector, as int64, on the current stream."""
@@ -145,11 +180,10 @@ class Exchange:
             raise ValueError("the peer all-reduce takes at most 1024 int32/int64 values")
         src = src.contiguous()
         out = torch.empty(n, dtype=torch.int64, device=self.dev)
-        self.epoch[RED_SLOT] += 1
+        e, e_dev = self._next_epoch(RED_SLOT)
         nat.call("eco_peer_allreduce_i64", src.data_ptr(), 32 if src.dtype == torch.int32 else 64, n,
                  0 if op == "max" else 1, self.red_ptrs, RED_STRIDE, self.red.t.data_ptr(), self.flag_ptrs,
-                 self.flags.t.data_ptr(), self.n, self.rank, RED_SLOT, self.epoch[RED_SLOT], out.data_ptr(),
-                 nat.stream())
+                 self.flags.t.data_ptr(), self.n, self.rank, RED_SLOT, e, e_dev, out.data_ptr(), nat.stream())
         return out
 
     def _after_current(self, stream) -> None:
@@ -169,10 +203,15 @@ class Exchange:
               slot: int) -> None:
         """One push kernel on the communication stream that signals ``slot`` when its stores are visible."""
         self._after_current(self.comm)
-        self.epoch[slot] += 1
+        e, e_dev = self._next_epoch(slot)
         nat.call("eco_peer_push_signal_s8", src, ld, rows, cols, dst, n_dst, ld_dst, row0, split, self.ctas,
-                 self.flag_ptrs, self.n, self.rank, slot, self.epoch[slot], self.tickets[slot].data_ptr(),
+                 self.flag_ptrs, self.n, self.rank, slot, e, e_dev, self.tickets[slot].data_ptr(),
                  self.comm.cuda_stream)
+        from . import graphs
+
+        g = graphs.capturing()
+        if g is not None:
+            g.join(self.comm)
 
     def push_input(self, bufs: LayerBufs, x: torch.Tensor) -> None:
         """This rank's input rows into every rank's ``x`` (rows rank * b ...)."""
@@ -191,6 +230,35 @@ class Exchange:
         w = bufs.w.t
         self._push(w.data_ptr() + lo * bufs.in_f, bufs.in_f, hi - lo, bufs.in_f, bufs.w_peers, self.n - 1,
                    bufs.in_f, lo, 0, bufs.slot_w)
+
+    def push_bias_rows(self, bufs: LayerBufs, lo: int, hi: int) -> None:
+        """This rank's rows of the bias column sums into the other ranks' ``gb``."""
+        nbytes = 8 * (hi - lo)
+        self._push(bufs.gb.t.data_ptr() + 8 * lo, nbytes, 1, nbytes, bufs.gb_peers, self.n - 1, nbytes, 0, 0,
+                   bufs.slot_gb)
+
+    def wait_bias_rows(self, bufs: LayerBufs, stream) -> None:
+        self.wait(bufs.slot_gb, stream)
+
+    def rowsum_buffer(self, rows: int) -> torch.Tensor:
+        """The optimizer's ``[world, rows]`` int64 row-sum buffer, mapped on every rank
+        (created on first use; collective)."""
+        if self.rowsum is None:
+            self.rowsum = Shared((self.n, rows), torch.int64, self.dev, self.group, self.maps)
+            self.rowsum_peers = _arr([p + 8 * rows * self.rank for r, p in enumerate(self.rowsum.ptrs)
+                                      if r != self.rank])
+        elif self.rowsum.t.shape[1] != rows:
+            raise RuntimeError("the peer exchange's row-sum buffer cannot change size")
+        return self.rowsum.t
+
+    def push_rowsum(self) -> None:
+        """This rank's row of the row-sum buffer into the other ranks' copies."""
+        nbytes = 8 * self.rowsum.t.shape[1]
+        self._push(self.rowsum.t[self.rank].data_ptr(), nbytes, 1, nbytes, self.rowsum_peers, self.n - 1, nbytes,
+                   0, 0, ROWSUM_SLOT)
+
+    def wait_rowsum(self) -> None:
+        self.wait(ROWSUM_SLOT, torch.cuda.current_stream(self.dev))
 
     def wait_weights(self, bufs: LayerBufs) -> None:
         self.wait(bufs.slot_w, torch.cuda.current_stream(self.dev))

@@ -75,7 +75,14 @@ def row_base() -> int:
     return _ROW_BASE
 
 
-def new_key() -> int:
+def new_key():
+    """A site's Philox key: drawn now from the generator, or -- while a ``StepGraph`` is
+    being captured -- a word of its table that every replay fills with a fresh draw."""
+    from . import graphs
+
+    g = graphs.capturing()
+    if g is not None:
+        return g.table.key()
     return int(torch.randint(0, 1 << 62, (1,), generator=_GEN).item())
 
 

@@ -156,6 +156,11 @@ def reduce_backward(dw_acc: torch.Tensor, gb_sum: torch.Tensor, amax: torch.Tens
 
 def start_dw_reduction(layer, dw_acc: torch.Tensor, gb_sum: torch.Tensor, s_g: float) -> None:
     """Launch the asynchronous dW / bias-sum reduction of one layer's backward."""
+    from . import graphs
+
+    if graphs.capturing() is not None:
+        raise RuntimeError("capturing a data-parallel step needs every layer row-sharded under the peer "
+                           f"exchange (a layer of {dw_acc.shape[0]} rows does not split over {world()} ranks)")
     out = dw_acc.shape[0]
     rows = shard_rows(out)
     if rows is None:
@@ -248,16 +253,18 @@ def start_dw_rows_peer(layer, g_i8: torch.Tensor, s_g: float) -> None:
     ex.push_grad_columns(bufs, _ops._rowmajor(g_i8))
     lo, hi = shard_rows(bufs.out)
     dws = ex.dw
+    ex._after_current(dws)  # the dW stream forks from this point of the step (and joins in finalize_pending)
     with torch.cuda.stream(dws):
         ex.wait(bufs.slot_x, dws)
         ex.wait(bufs.slot_dy, dws)
         amax = torch.empty(1, dtype=torch.int32, device=bufs.x.t.device)
         red = _ops.gemm_s32(bufs.dy.t, 1, bufs.x.t, 1, hi - lo, bufs.in_f, bufs.x.t.shape[0], amax=amax)
-        gb = torch.zeros(bufs.out, dtype=torch.int64, device=red.device)  # other rows: the flat SUM
+        gb = bufs.gb.t  # this rank's rows here; the other ranks store theirs
         _ops.colsum(bufs.dy.t, out=gb[lo:hi])
+        ex.push_bias_rows(bufs, lo, hi)
         bufs.done.record(dws)
     layer._dw_pending = {"red": red, "full": None, "shape": (bufs.out, bufs.in_f), "work": None, "gb": gb,
-                         "event": bufs.done, "rows": (lo, hi), "s_g": s_g, "amax": amax}
+                         "event": bufs.done, "rows": (lo, hi), "s_g": s_g, "amax": amax, "peer": bufs}
     _PENDING.append(layer)
 
 
@@ -333,16 +340,20 @@ def finalize_pending() -> None:
         p = l._dw_pending
         if p.get("event") is not None:
             cur.wait_event(p["event"])
-            for t in (p["red"], p["amax"], p["gb"]):
+            for t in (p["red"], p["amax"]):
                 t.record_stream(cur)
-    # the bias column sums of every pending layer in one all-reduce
-    gbs = [l._dw_pending["gb"] for l in layers]
-    flat = torch.cat(gbs)
-    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=_SMALL)
-    off = 0
-    for l, g in zip(layers, gbs):
-        l._dw_pending["gb"] = flat[off:off + g.numel()]
-        off += g.numel()
+        if p.get("peer") is not None:  # the other ranks' rows of the bias sums have arrived
+            _PEER.wait_bias_rows(p["peer"], cur)
+    # the bias column sums of the other pending layers in one all-reduce
+    summed = [l for l in layers if l._dw_pending.get("peer") is None]
+    if summed:
+        gbs = [l._dw_pending["gb"] for l in summed]
+        flat = torch.cat(gbs)
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=_SMALL)
+        off = 0
+        for l, g in zip(summed, gbs):
+            l._dw_pending["gb"] = flat[off:off + g.numel()]
+            off += g.numel()
     for layer in layers:
         if layer._dw_pending["work"] is not None:
             layer._dw_pending["work"].wait()
@@ -390,8 +401,26 @@ def gather_rows(layer, rows) -> None:
                                                        async_op=True)]
 
 
+def flat_buffer(shape, device) -> torch.Tensor:
+    """The rank-major ``[world, k]`` int64 buffer of ``gather_flat`` (mapped on every rank
+    under the peer exchange)."""
+    if _PEER is not None:
+        return _PEER.rowsum_buffer(shape[1])
+    return torch.empty(shape, dtype=torch.int64, device=device)
+
+
+class _PeerGather:
+    """The handle of a peer row-sum gather: ``wait`` orders the current stream after it."""
+
+    def wait(self) -> None:
+        _PEER.wait_rowsum()
+
+
 def gather_flat(flat: torch.Tensor):
     """All-gather a rank-major ``[world, k]`` buffer whose row ``rank()`` this rank filled."""
+    if _PEER is not None and _PEER.rowsum is not None and flat.data_ptr() == _PEER.rowsum.t.data_ptr():
+        _PEER.push_rowsum()
+        return _PeerGather()
     return dist.all_gather_into_tensor(flat, flat[rank()], group=_SMALL, async_op=True)
 
 

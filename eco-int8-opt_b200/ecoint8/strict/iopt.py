@@ -179,13 +179,16 @@ class I8ECO:
         self._state = st.to(dev)
         self._counter = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    def _raise_pending(self, block: bool) -> None:
+    def _raise_pending(self, block: bool, idle: bool = False) -> None:
+        """Raise the error a finished step flagged.  ``idle``: the device is known to be
+        idle (no event calls, e.g. while a graph is being captured)."""
         if self._err is None:
             return
         event, flags, sflags = self._err
-        if not block and not event.query():
-            return
-        event.synchronize()
+        if not idle:
+            if not block and not event.query():
+                return
+            event.synchronize()
         self._err = None
         if int(sflags[0]):  # a device scale of the queued backward overflowed (the reference raises there)
             _scale.raise_flags(self._state.device)
@@ -206,19 +209,33 @@ class I8ECO:
         return _ops.sumsq(g)
 
     # -- step ------------------------------------------------------------
-    @torch.no_grad()
-    def step(self):
-        t0 = time.perf_counter()
-        self._raise_pending(block=True)  # the previous step's flags (long since copied back)
-        HOST_WAIT_S[0] += time.perf_counter() - t0
+    def _hyper(self, replay: bool, dp: bool) -> "nat.I8ECOHyper":
+        """The launch's hyper-parameters from the current lr and momentum (iopt.py:104-110)."""
         b = self.beta
         alpha = (1.0 / self.lr) * (1.0 - 1.0 / b)
-        b_q = round(b * BETA_Q)
-        nb_q = round((1.0 - b) * BETA_Q)
-        lr_q = round(self.lr * LR_Q)
-        a_q = round(alpha * BETA_Q)
-        self.step_count += 1
-        F = FRAC_BITS
+        hyper = nat.I8ECOHyper()
+        hyper.lr = self.lr
+        hyper.grad_clip = -1.0 if self.grad_clip is None else float(self.grad_clip)
+        hyper.b_q, hyper.nb_q = round(b * BETA_Q), round((1.0 - b) * BETA_Q)
+        hyper.lr_q, hyper.a_q = round(self.lr * LR_Q), round(alpha * BETA_Q)
+        hyper.sr_mode = nat.SR_REPLAY32 if replay else nat.SR_PHILOX
+        hyper.finalize = 0 if dp else 1  # under data parallelism: max over the row shards first
+        hyper.done_counter = self._counter.data_ptr()
+        return hyper
+
+    @torch.no_grad()
+    def step(self):
+        from .. import graphs
+
+        graph = graphs.capturing()
+        t0 = time.perf_counter()
+        if graph is None:
+            self._raise_pending(block=True)  # the previous step's flags (long since copied back)
+        else:  # capture starts on an idle device: the last eager step's flags are in
+            self._raise_pending(block=True, idle=True)
+        HOST_WAIT_S[0] += time.perf_counter() - t0
+        if graph is None:
+            self.step_count += 1
         active = [(i, layer) for i, layer in enumerate(self.layers) if layer._gw_i8 is not None]
         if not active:
             return
@@ -268,14 +285,19 @@ class I8ECO:
             if replay:
                 keep += self._replay_nudges(d, layer, s_m_now[i], s_g, gsq, (out, rowlen), lo)
             keep += [g, gsq] + ([s_g_raw.t] if queued_g else [])
-        hyper = nat.I8ECOHyper()
-        hyper.lr = self.lr
-        hyper.grad_clip = -1.0 if self.grad_clip is None else float(self.grad_clip)
-        hyper.b_q, hyper.nb_q, hyper.lr_q, hyper.a_q = b_q, nb_q, lr_q, a_q
-        hyper.sr_mode = nat.SR_REPLAY32 if replay else nat.SR_PHILOX
-        hyper.finalize = 0 if dp else 1  # under data parallelism: max over the row shards first
-        hyper.seed = 0 if replay else _sr.new_key()
-        hyper.done_counter = self._counter.data_ptr()
+        hyper = self._hyper(replay, dp)
+        key = 0 if replay else _sr.new_key()
+        if isinstance(key, graphs.DevKey):
+            # a replayed step reads the lr and key of the moment from the graph's table
+            def image(table, key=key, replay=replay, dp=dp):
+                h = self._hyper(replay, dp)
+                h.seed = table.value(key.off)
+                return h
+
+            hyper.seed = 0
+            hyper.dev = graph.table.block((ctypes.sizeof(nat.I8ECOHyper) + 7) // 8, graphs.struct_fill(image))
+        else:
+            hyper.seed = key
         if _sr.LOG is not None and not replay:
             _sr.LOG.append(("i8eco_step", hyper.seed, [(i, 2 * i, 2 * i + 1) for i, _ in active]))
         self._keep_plan = plan
@@ -289,15 +311,38 @@ class I8ECO:
                     parallel.gather_rows(layer, rows)
             if plan["flat"] is not None:
                 self._rowsum_work = parallel.gather_flat(plan["flat"])
-        self._pending_stats = [(src, layer.sw.snapshot(), layer.w_i8.shape[1], layer.out_features)
-                               for (_, layer), src in zip(active, plan["rowsum"])]
+        pending = [(src, layer.sw.snapshot(), layer.w_i8.shape[1], layer.out_features)
+                   for (_, layer), src in zip(active, plan["rowsum"])]
         # error flags come back asynchronously into one of two persistent pinned buffers
-        # (allocating pinned memory every step can stall the host)
+        # (allocating pinned memory every step can stall the host); a third one is a
+        # captured graph's
         if getattr(self, "_flag_bufs", None) is None or self._flag_bufs[0][0].numel() != len(self.layers):
             self._flag_bufs = [(torch.empty(len(self.layers), dtype=torch.int64, pin_memory=True),
                                 torch.empty(1, dtype=torch.int32, pin_memory=True),
-                                torch.cuda.Event()) for _ in range(2)]
+                                torch.cuda.Event()) for _ in range(3)]
             self._flag_turn = 0
+        if graph is not None:
+            flags, sflags, _ = self._flag_bufs[2]
+            flags.copy_(self._state[:, 2], non_blocking=True)
+            sflags.copy_(_scale.flags(dev), non_blocking=True)
+            work = self._rowsum_work
+
+            def after_replay(flags=flags, sflags=sflags, pending=pending, work=work, keep=keep):
+                if self._err is not None:  # the previous replay's flags (bounds the host's lead)
+                    t0 = time.perf_counter()
+                    self._raise_pending(block=True)
+                    HOST_WAIT_S[0] += time.perf_counter() - t0
+                self.step_count += 1
+                ev = torch.cuda.Event()
+                ev.record()
+                self._err = (ev, flags, sflags)
+                self._pending_stats = pending
+                self._rowsum_work = work
+                self._keep = keep
+
+            graph.on_replay(after_replay)
+            return
+        self._pending_stats = pending
         flags, sflags, ev = self._flag_bufs[self._flag_turn]
         self._flag_turn ^= 1
         t0 = time.perf_counter()
@@ -327,7 +372,7 @@ class I8ECO:
         if plan is not None and plan["key"] == key:
             return plan
         shard_total = sum(r[1] - r[0] for r in (getattr(l, "_gw_rows", None) for _, l in active) if r is not None)
-        flat = torch.empty((world, shard_total), dtype=torch.int64, device=dev) if dp and shard_total else None
+        flat = parallel.flat_buffer((world, shard_total), dev) if dp and shard_total else None
         descs, rows_l, rowsum_l = [], [], []
         off = 0
         for i, layer in active:

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define ECO_ABI_VERSION 3
+#define ECO_ABI_VERSION 4
 
 enum {
   ECO_OK = 0,
@@ -55,8 +55,19 @@ enum {
 };
 
 /* ECO_SR_REPLAY_F32: fp32 uniforms in [0, 1) at nudge[row * nudge_ld + col] (a
- * torch.rand_like draw, quant.py:25); only the loss-boundary entry point takes it. */
-enum { ECO_SR_NEAREST = 0, ECO_SR_PHILOX = 1, ECO_SR_REPLAY32 = 2, ECO_SR_REPLAY64 = 3, ECO_SR_REPLAY_F32 = 4 };
+ * torch.rand_like draw, quant.py:25); only the loss-boundary entry point takes it.
+ * ECO_SR_PHILOX_DEV: ECO_SR_PHILOX with the key read from device memory when the
+ * kernel runs -- the uint64 word at `nudge` (8-byte aligned) instead of `seed` -- so a
+ * captured CUDA graph replays the launch with whatever key that word holds then.
+ * The requant, fused-GEMM and loss-boundary entry points take it. */
+enum {
+  ECO_SR_NEAREST = 0,
+  ECO_SR_PHILOX = 1,
+  ECO_SR_REPLAY32 = 2,
+  ECO_SR_REPLAY64 = 3,
+  ECO_SR_REPLAY_F32 = 4,
+  ECO_SR_PHILOX_DEV = 5,
+};
 
 typedef void* eco_stream_t; /* cudaStream_t */
 
@@ -241,11 +252,14 @@ ECO_API int eco_peer_push_s8(const int8_t* src, int64_t ld_src, int64_t rows, in
  * fenced at system scope, the last CTA writes epoch into entry (slot, rank) of the
  * n_ranks flag arrays (as eco_peer_signal; one launch instead of two).  ticket: a
  * device word, zero before the call (the kernel leaves it zero), one per call in
- * flight. */
+ * flight.
+ * epoch_dev (here and in the calls below, nullable): a device word read when the kernel
+ * runs, in place of `epoch` -- a captured CUDA graph replays the exchange with the
+ * epochs of the moment. */
 ECO_API int eco_peer_push_signal_s8(const int8_t* src, int64_t ld_src, int64_t rows, int64_t cols,
                             int8_t* const* dst, int n_dst, int64_t ld_dst, int64_t dst_row0, int split, int ctas,
                             int64_t* const* peer_flags, int n_ranks, int rank, int slot, int64_t epoch,
-                            uint32_t* ticket, eco_stream_t stream);
+                            const int64_t* epoch_dev, uint32_t* ticket, eco_stream_t stream);
 
 /* All-reduce (op 0: MAX, 1: SUM, int64 arithmetic) of count <= stride values (int32 or
  * int64 at src) over the n ranks, result int64[count] in out.  bufs: the n ranks'
@@ -254,8 +268,8 @@ ECO_API int eco_peer_push_signal_s8(const int8_t* src, int64_t ld_src, int64_t r
  * (5 s; then out is zero and the error bit is set). */
 ECO_API int eco_peer_allreduce_i64(const void* src, int src_bits, int count, int op, int64_t* const* bufs,
                            int stride, const int64_t* own_buf, int64_t* const* peer_flags,
-                           const int64_t* own_flags, int n, int rank, int slot, int64_t epoch, int64_t* out,
-                           eco_stream_t stream);
+                           const int64_t* own_flags, int n, int rank, int slot, int64_t epoch,
+                           const int64_t* epoch_dev, int64_t* out, eco_stream_t stream);
 
 /* Flag arrays are int64 [slots, ECO_MAX_PEERS], zero before first use.  signal:
  * after all prior work on the stream, writes epoch into entry (slot, rank) of
@@ -264,9 +278,9 @@ ECO_API int eco_peer_allreduce_i64(const void* src, int src_bits, int count, int
  * all reach epoch (epochs only grow), or after timeout_us (0: the 5 s limit;
  * larger values are capped at it). */
 ECO_API int eco_peer_signal(int64_t* const* peer_flags, int n, int rank, int slot, int64_t epoch,
-                    eco_stream_t stream);
-ECO_API int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, int64_t timeout_us,
-                  eco_stream_t stream);
+                    const int64_t* epoch_dev, eco_stream_t stream);
+ECO_API int eco_peer_wait(const int64_t* flags, int n, int slot, int64_t epoch, const int64_t* epoch_dev,
+                  int64_t timeout_us, eco_stream_t stream);
 
 /* Mapping the exchange buffers between the processes of one node (CUDA IPC).
  * export: the IPC handle (ECO_IPC_HANDLE_BYTES bytes at `handle`) of the device
@@ -323,7 +337,7 @@ typedef struct {
   const int64_t* s_gb_dev; /* nullable: likewise for s_gb */
 } eco_i8eco_layer_t;
 
-typedef struct {
+typedef struct eco_i8eco_hyper {
   double lr;
   double grad_clip;     /* < 0: no clipping (grad_clip=None) */
   int64_t b_q, nb_q, lr_q, a_q; /* iopt.py:107-110 */
@@ -332,6 +346,10 @@ typedef struct {
                            (state[1]) for eco_i8eco_finalize, e.g. after a cross-rank max */
   uint64_t seed;
   uint32_t* done_counter; /* device word, zero between steps (reset by the kernel) */
+  const struct eco_i8eco_hyper* dev; /* nullable: a copy of this struct in device memory whose
+                             lr, grad_clip, b_q, nb_q, lr_q, a_q and seed the kernel reads when
+                             it runs, in place of the values above (a captured CUDA graph then
+                             replays the step with the learning rate and key of the moment) */
 } eco_i8eco_hyper_t;
 
 ECO_API int eco_i8eco_step(const eco_i8eco_layer_t* layers, int n_layers, const eco_i8eco_hyper_t* hyper,

@@ -143,3 +143,115 @@ def test_two_gpu_data_parallel_equals_single_gpu():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert ok == {"reduce": True, "gather": True, "peer": True, "peer+fused": True}
+
+
+# ---------------------------------------------------------------------------- CUDA graphs
+GH, GC = 48, 16  # every layer splits into row shards of at least 8 over 2 ranks
+
+
+def _graph_net(dev):
+    from ecoint8 import I8Linear, I8ReLU, I8Sequential
+
+    torch.manual_seed(0)
+    return I8Sequential(I8Linear(D, GH), I8ReLU(), I8Linear(GH, GH), I8ReLU(), I8Linear(GH, GC)).to(dev)
+
+
+def _graph_train(net, x8, sx, y, row_base, steps, graph):
+    """``steps`` steps of the fused-boundary loop, eagerly or as one eager step plus
+    replays of a captured graph, with a changing learning rate."""
+    from ecoint8 import I8ECO
+    from ecoint8._sr import batch_rows, set_generator
+    from ecoint8.graphs import StepGraph
+    from ecoint8.quant import cross_entropy_grad_i8
+
+    set_generator(torch.Generator().manual_seed(321))
+    with batch_rows(row_base):
+        net.calibrate(x8, sx)
+        opt = I8ECO(net.int8_layers(), lr=0.3, momentum=0.9)
+
+        def step():
+            logits, s_out = net.forward_i8(x8)
+            loss, g8, sg = cross_entropy_grad_i8(logits, s_out, y, count=B)
+            net.backward_i8(g8, sg)
+            opt.step()
+            opt.zero_grad()
+            return loss
+
+        g = StepGraph(step, warmup=1) if graph else None
+        for t in range(steps):
+            opt.set_lr(0.3 - 0.02 * t)
+            if g is None:
+                step()
+            elif t == 0:
+                g.capture()
+            else:
+                g.replay()
+    set_generator(None)
+    return opt
+
+
+def _graph_worker(rank, port, q):
+    import sys
+
+    sys.path[:0] = [os.environ["ECO_PKG"], os.environ["ECO_REPO"]]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from ecoint8 import parallel
+        from ecoint8.quant import quantize_tensor_dynamic
+
+        gen = torch.Generator().manual_seed(8)
+        X = torch.randn(B, D, generator=gen) * 2.0
+        Y = torch.randint(0, GC, (B,), generator=gen)
+        X8, sx = quantize_tensor_dynamic(X)
+        lo, hi = rank * B // 2, (rank + 1) * B // 2
+        parallel.init(dw_exchange="peer")
+        net = _graph_net(dev)
+        opt = _graph_train(net, X8[lo:hi].to(dev), sx, Y[lo:hi].to(dev), lo, 5, graph=True)
+        parallel.synchronize(net.int8_layers())
+        parallel.gather_momentum(opt)
+        stats = opt.stats["mean_abs_e"]
+        steps = opt.step_count
+        parallel.shutdown()
+        if rank == 0:
+            single = _graph_net(dev)
+            sopt = _graph_train(single, X8.to(dev), sx, Y.to(dev), 0, 5, graph=False)
+            ok = all(torch.equal(a.w_i8, b.w_i8) for a, b in zip(net.int8_layers(), single.int8_layers()))
+            ok &= all(torch.equal(a.b_acc, b.b_acc) for a, b in zip(net.int8_layers(), single.int8_layers()))
+            ok &= all(torch.equal(a, b) for a, b in zip(opt.m_i8, sopt.m_i8))
+            ok &= opt.s_m == sopt.s_m
+            ok &= stats == sopt.stats["mean_abs_e"]
+            ok &= steps == sopt.step_count == 5
+            q.put(bool(ok))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_graph_replay_equals_single_gpu():
+    """The data-parallel step (peer exchange) captured as a CUDA graph on each rank and
+    replayed reproduces the single-GPU eager run bit for bit."""
+    import pathlib
+
+    import torch.multiprocessing as mp
+
+    repo = pathlib.Path(__file__).resolve().parent.parent
+    os.environ["ECO_PKG"] = str(repo / "eco-int8-opt_b200")
+    os.environ["ECO_REPO"] = str(repo)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_graph_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    ok = q.get(timeout=300)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert ok

@@ -24,7 +24,7 @@ def test_library_loads_and_exports_every_header_symbol():
     for n in names:
         assert hasattr(lib, n), n
     assert sorted(names) == sorted(_native.exported_symbols())
-    assert lib.eco_abi_version() == 3
+    assert lib.eco_abi_version() == 4
 
 
 def test_c_abi_rejects_bad_arguments_with_a_message():
