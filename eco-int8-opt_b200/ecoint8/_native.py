@@ -50,6 +50,20 @@ class I8ECOHyper(ctypes.Structure):
                 ("dev", c_p)]
 
 
+class Fp32Layer(ctypes.Structure):
+    """``eco_fp32_layer_t``."""
+
+    _fields_ = [("w", c_p), ("m", c_p), ("v", c_p), ("g", c_p), ("sw", c_p), ("s_fixed", c_p), ("u", c_p),
+                ("rows", c_i64), ("cols", c_i64), ("stream", c_u64), ("norm_out", c_p), ("stepped_out", c_p)]
+
+
+class Fp32Hyper(ctypes.Structure):
+    """``eco_fp32_hyper_t``."""
+
+    _fields_ = [("kind", c_i32), ("sr_mode", c_i32), ("lr", c_d), ("beta1", c_d), ("beta2", c_d), ("eps", c_d),
+                ("weight_decay", c_d), ("grad_clip", c_d), ("bc1", c_d), ("bc2", c_d), ("seed", c_u64)]
+
+
 # name -> (restype, argtypes); one line per entry point of the header
 _SIGS = {
     "eco_abi_version": (c_i32, []),
@@ -90,6 +104,8 @@ _SIGS = {
     "eco_i8eco_step": (c_i32, [ctypes.POINTER(I8ECOLayer), c_i32, ctypes.POINTER(I8ECOHyper), c_p]),
     "eco_i8eco_finalize": (c_i32, [c_p, c_i32, c_p]),
     "eco_sgdm_step": (c_i32, [c_p, c_p, c_p, c_i64, c_i64, c_p, c_p, c_f, c_f, c_f, c_f, c_u64, c_p, c_p]),
+    "eco_fp32_eco_step": (c_i32, [ctypes.POINTER(Fp32Layer), c_i32, ctypes.POINTER(Fp32Hyper), c_p, c_i64, c_p]),
+    "eco_fp32_eco_scratch_len": (c_i64, [ctypes.POINTER(Fp32Layer), c_i32]),
 }
 
 _lib = None

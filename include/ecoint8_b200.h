@@ -371,6 +371,53 @@ ECO_API int eco_sgdm_step(int8_t* w, int8_t* m, const float* g, int64_t rows, in
                   const float* sw, float* sm, float lr, float beta, float wd, float alpha,
                   uint64_t seed, uint32_t* scratch, eco_stream_t stream);
 
+/* ------------------------------------------------- EcoSGDM / EcoAdam steps -----
+ * The fp32-state ECO optimizers (ecoint8/eco.py:50-235) over a list of layers in two
+ * launches, replacing the per-layer PyTorch loops of EcoSGDM.step (:94-131) and
+ * EcoAdam.step (:182-228) with their .item() syncs (g.norm(), e.abs().mean()):
+ *   1. per layer: the gradient norm (double sum of squares) and whether every
+ *      gradient value is finite (_get_grad_w, :39-47);
+ *   2. per element: clip, weight decay, moment update(s), stochastic rounding onto the
+ *      frozen grid (quant.py:19-28), error injection; w and m (v) updated in place.
+ * Each fp32 operation is the reference's PyTorch operation with PyTorch's CUDA
+ * rounding (a Python scalar operand rounded to fp32; add with alpha and addcmul as a
+ * fused multiply-add; division by a Python scalar as a multiply by the fp32
+ * reciprocal; scalar / tensor as reciprocal times scalar).  The norm is the fp32
+ * rounding of the square root of the double sum of squares.
+ * scratch: device doubles, at least eco_fp32_eco_scratch_len() of them; on return
+ * scratch[2*T + t] holds sum |e| of tile t of 65536 elements (layers in order, their
+ * tiles in order), T = the number of tiles (the statistics' inputs). */
+typedef struct {
+  int8_t* w;             /* [rows, cols] int8 weights, updated in place */
+  float* m;              /* [rows, cols] fp32 momentum / first moment, updated in place */
+  float* v;              /* [rows, cols] fp32 second moment (Adam), updated in place; else NULL */
+  const float* g;        /* [rows, cols] fp32 weight gradient (layer._grad_w) */
+  const float* sw;       /* [rows] the layer's row scales s_w (w_fp32 = w * s_w) */
+  const float* s_fixed;  /* [rows] the optimizer's frozen grid (the s_w clone taken at construction) */
+  const float* u;        /* ECO_SR_REPLAY_F32: [rows, cols] uniforms in [0, 1); else NULL */
+  int64_t rows, cols;
+  uint64_t stream;       /* Philox site of the layer's rounding */
+  float* norm_out;       /* nullable: the gradient norm, fp32 */
+  int32_t* stepped_out;  /* nullable: 1 if the layer was stepped, 0 if skipped (non-finite gradient) */
+} eco_fp32_layer_t;
+
+typedef struct {
+  int32_t kind;          /* 0: EcoSGDM, 1: EcoAdam */
+  int32_t sr_mode;       /* ECO_SR_PHILOX or ECO_SR_REPLAY_F32 */
+  double lr;
+  double beta1;          /* EcoSGDM: momentum; EcoAdam: betas[0] */
+  double beta2, eps;     /* EcoAdam */
+  double weight_decay;
+  double grad_clip;      /* < 0: no clipping (grad_clip=None) */
+  double bc1, bc2;       /* EcoAdam: 1 - beta1^t, 1 - beta2^t (eco.py:184) */
+  uint64_t seed;         /* Philox key (ECO_SR_PHILOX) */
+} eco_fp32_hyper_t;
+
+ECO_API int eco_fp32_eco_step(const eco_fp32_layer_t* layers, int n_layers, const eco_fp32_hyper_t* hyper,
+                              double* scratch, int64_t scratch_len, eco_stream_t stream);
+/* The scratch length (doubles) eco_fp32_eco_step needs for these layers (<= 0 on bad input). */
+ECO_API int64_t eco_fp32_eco_scratch_len(const eco_fp32_layer_t* layers, int n_layers);
+
 #ifdef __cplusplus
 }
 #endif

@@ -345,6 +345,63 @@ def gen_sgdm_triton(ref):
     return cases
 
 
+FP32_CASES = [  # (optimizer, layer shapes, steps, weight decay, grad clip, seed)
+    ("sgdm", [(24, 40), (16, 24)], 3, 0.0, 1.0, 11),
+    ("sgdm", [(24, 40), (16, 24)], 3, 0.01, 0.05, 12),  # clipping active, weight decay
+    ("adam", [(24, 40), (16, 24)], 3, 0.0, 1.0, 13),
+    ("adam", [(24, 40), (16, 24)], 3, 0.01, 0.05, 14),
+]
+
+
+def fp32_case_inputs(layer_cls, shapes, steps, seed, torch):
+    """The seeded inputs of an fp32-optimizer case: layers, then per step the gradients
+    (the uniforms of the stochastic rounding follow inside each step, one
+    ``torch.rand_like`` per layer, from the same generator)."""
+    torch.manual_seed(seed)
+    layers = [layer_cls(i, o) for (o, i) in shapes]
+    return layers
+
+
+def gen_fp32_eco(ref):
+    """EcoSGDM / EcoAdam (eco.py:50-235) on the reference's Int8Linear layers, on CPU.
+    The uniforms each step draws (quant.py:25, torch.rand_like) are logged."""
+    import torch
+
+    eco, Int8Linear = ref["eco"], ref["Int8Linear"]
+    cases = []
+    for kind, shapes, steps, wd, clip, seed in FP32_CASES:
+        layers = fp32_case_inputs(Int8Linear, shapes, steps, seed, torch)
+        w0 = [l.w_i8.clone() for l in layers]
+        opt = (eco.EcoSGDM(layers, lr=0.05, momentum=0.9, weight_decay=wd, grad_clip=clip) if kind == "sgdm"
+               else eco.EcoAdam(layers, lr=1e-3, weight_decay=wd, grad_clip=clip))
+        per_step = []
+        for t in range(steps):
+            for l in layers:
+                l._grad_w = torch.randn(l.w_i8.shape) * 0.02
+            drawn = []
+            orig = torch.rand_like
+
+            def logged(x, *a, **k):
+                r = orig(x, *a, **k)
+                drawn.append(digest(r))
+                return r
+
+            torch.rand_like = logged
+            try:
+                opt.step()
+            finally:
+                torch.rand_like = orig
+            state = {"w": [digest(l.w_i8) for l in layers], "m": [digest(m) for m in opt.m],
+                     "mean_abs_e": fhex(opt.stats["mean_abs_e"]), "u": drawn}
+            if kind == "adam":
+                state["v"] = [digest(v) for v in opt.v]
+            per_step.append(state)
+            opt.zero_grad()
+        cases.append({"kind": kind, "shapes": shapes, "steps": steps, "wd": wd, "clip": clip, "seed": seed,
+                      "w0": [digest(w) for w in w0], "trace": per_step})
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ECOINT8_REFERENCE"),
@@ -364,13 +421,15 @@ def main():
     import ecoint8.fixedpoint as fixedpoint
     import ecoint8.strict.ilayer as ilayer
     import ecoint8.strict.iopt as iopt
+    import ecoint8.eco as eco
+    import ecoint8.layers as layers
     import ecoint8.triton_kernels as triton_kernels
     from oracle import boundary as bnd
 
     assert pathlib.Path(ecoint8.__file__).resolve().is_relative_to(pathlib.Path(args.reference).resolve())
     ref = {"fixedpoint": fixedpoint, "ilayer": ilayer, "iopt": iopt, "triton_kernels": triton_kernels,
            "I8Linear": ilayer.I8Linear, "I8ReLU": ilayer.I8ReLU, "I8Sequential": ilayer.I8Sequential,
-           "I8ECO": iopt.I8ECO}
+           "I8ECO": iopt.I8ECO, "eco": eco, "Int8Linear": layers.Int8Linear}
     gens = {
         "fixedpoint.json": lambda: gen_fixedpoint(ref),
         "blob_train.json": lambda: gen_blob(ref, bnd, args.epochs),
@@ -379,6 +438,7 @@ def main():
         "eco_step.json": lambda: gen_eco_step(ref),
         "sgdm_triton.json": lambda: gen_sgdm_triton(ref),
         "wide_train.json": lambda: gen_wide(ref, bnd, 2),
+        "fp32_eco.json": lambda: gen_fp32_eco(ref),
     }
     if args.only:
         torch.set_num_threads(os.cpu_count() or 1)  # the wide fixture's GEMMs (results do not depend on it)

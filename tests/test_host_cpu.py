@@ -59,6 +59,13 @@ def test_no_cpu_path_fails_loudly():
     lin._gw_s = 1e-3
     with pytest.raises(RuntimeError, match="CUDA"):
         I8ECO([lin]).step()
+    from ecoint8 import EcoAdam, EcoSGDM, Int8Linear
+
+    fl = Int8Linear(16, 8)
+    fl._grad_w = torch.zeros(8, 16)
+    for opt in (EcoSGDM([fl]), EcoAdam([fl])):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            opt.step()
 
 
 STRICT = ["fixedpoint.py", "strict/ilayer.py", "strict/iopt.py"]
@@ -89,8 +96,9 @@ def test_public_api_matches_reference_surface():
     for name in ["calc_scale", "quantize_symmetric", "quantize_tensor_dynamic", "quantize_per_channel",
                  "dequantize", "saturation_ratio"]:
         assert hasattr(quant, name), name
-    with pytest.raises(NotImplementedError):
-        ecoint8.EcoSGDM([])
+    # the fp32-state optimizers construct like the reference's
+    assert ecoint8.EcoSGDM([]).stats == {"skipped": 0, "mean_abs_e": 0.0}
+    assert ecoint8.EcoAdam([], lr=1e-3).t == 0
 
 
 def test_scalar_bookkeeping_is_the_reference_arithmetic():
