@@ -67,6 +67,14 @@ struct GemmParams {
   int8_t* Y;
   i64 ldy;
   PhiloxKeys keys;  // round keys of sr.seed
+  // fp32 dequant epilogue: Yf = fp32(C) * fp32(sa * sb) * col_scale[n] + bias_f[n]
+  float* Yf;
+  i64 ldyf;
+  const int64_t* sa_dev;  // nullable: sa as double bits on the device
+  const int64_t* sb_dev;  // nullable: sb as double bits on the device
+  double sa, sb;
+  const float* col_scale;  // nullable
+  const float* bias_f;     // nullable
 };
 
 // Tile t of the grouped raster: kGroupM M-tiles share each N column block in turn.
@@ -272,6 +280,32 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const eco_sr_t& sr, const Ph
   }
 }
 
+// fp32 dequant epilogue for one 32-column chunk of one row (Int8LinearFunc, layers.py:
+// 49-52, 64, 67): fp32(acc) * scalar, then * col_scale[n], then + bias[n], each one IEEE
+// fp32 operation like PyTorch's kernels; the scalar is the fp32 rounding of the double
+// product sa * sb (a Python float, or a product of two, in the reference).
+ECO_DEV void epi_store_dequant(const GemmParams& p, float scalar, const uint32_t (&v)[32], int m, int nb,
+                               float cs_lane, float bias_lane) {
+  float o[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) {  // every lane shuffles (row m may be past the end)
+    float y = __fmul_rn(__int2float_rn((int)v[e]), scalar);
+    if (p.col_scale) y = __fmul_rn(y, __shfl_sync(0xffffffffu, cs_lane, e));
+    if (p.bias_f) y = __fadd_rn(y, __shfl_sync(0xffffffffu, bias_lane, e));
+    o[e] = y;
+  }
+  if (m >= p.M) return;
+  float* dst = p.Yf + (i64)m * p.ldyf + nb;
+  if (nb + 32 <= p.N && (p.ldyf & 3) == 0 && (reinterpret_cast<uintptr_t>(p.Yf) & 15) == 0) {
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (nb + e < p.N) dst[e] = o[e];
+  }
+}
+
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -397,6 +431,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     int j = 0;
     PhiloxKeys keys;
     const eco_sr_t sr = sr_resolve(p.sr, p.keys, keys);
+    float scalar = 0.0f;
+    if (EPI == 2) {
+      const double a = p.sa_dev ? __longlong_as_double(*p.sa_dev) : p.sa;
+      const double b = p.sb_dev ? __longlong_as_double(*p.sb_dev) : p.sb;
+      scalar = __double2float_rn(__dmul_rn(a, b));
+    }
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++j) {
       const int b = j & 1;
       if (!mbar_wait(&tfull[b], (uint32_t)(j >> 1) & 1u) || *abort_flag) {
@@ -415,6 +455,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + (uint32_t)(b * BN + col) + ((uint32_t)(q * 32) << 16), v);
         if (nb >= p.N) continue;  // warp-uniform
         const int n_lane = nb + lane;
+        if (EPI == 2) {
+          const float cs = (p.col_scale && n_lane < p.N) ? __ldg(p.col_scale + n_lane) : 0.0f;
+          const float bf = (p.bias_f && n_lane < p.N) ? __ldg(p.bias_f + n_lane) : 0.0f;
+          epi_store_dequant(p, scalar, v, m, nb, cs, bf);
+          continue;
+        }
         const int bias_lane = (p.bias && n_lane < p.N) ? __ldg(p.bias + n_lane) : 0;
         if (EPI == 0) {
           epi_store_s32(p, v, m, nb, bias_lane, amax);
@@ -516,8 +562,8 @@ int gemm_common(const int8_t* A, i64 lda, int a_layout, const int8_t* B, i64 ldb
   if (int rc = a_layout ? make_tmap(&ta, A, M, K, lda, 128, BK) : make_tmap(&ta, A, K, M, lda, BK, BM)) return rc;
   if (int rc = b_layout ? make_tmap(&tb, B, N, K, ldb, 128, BK) : make_tmap(&tb, B, K, N, ldb, BK, BN)) return rc;
   if (BN == 128)
-    return epi ? launch<128, 1>(ta, tb, p, s) : launch<128, 0>(ta, tb, p, s);
-  return epi ? launch<256, 1>(ta, tb, p, s) : launch<256, 0>(ta, tb, p, s);
+    return epi == 2 ? launch<128, 2>(ta, tb, p, s) : epi ? launch<128, 1>(ta, tb, p, s) : launch<128, 0>(ta, tb, p, s);
+  return epi == 2 ? launch<256, 2>(ta, tb, p, s) : epi ? launch<256, 1>(ta, tb, p, s) : launch<256, 0>(ta, tb, p, s);
 }
 
 }  // namespace
@@ -552,6 +598,23 @@ extern "C" int eco_gemm_s8_requant(const int8_t* A, int64_t lda, int a_layout, c
   p.Y = Y;
   p.ldy = ldy;
   return gemm_common(A, lda, a_layout, B, ldb, b_layout, M, N, K, p, 1, eco_stream(stream), "eco_gemm_s8_requant");
+}
+
+extern "C" int eco_gemm_s8_dequant(const int8_t* A, int64_t lda, int a_layout, const int8_t* B, int64_t ldb,
+                                   int b_layout, int64_t M, int64_t N, int64_t K, const int64_t* sa_dev, double sa,
+                                   const int64_t* sb_dev, double sb, const float* col_scale, const float* bias,
+                                   float* Y, int64_t ldy, eco_stream_t stream) {
+  ECO_REQUIRE(Y && ldy >= N, ECO_ERR_ARG, "eco_gemm_s8_dequant: bad output");
+  GemmParams p{};
+  p.Yf = Y;
+  p.ldyf = ldy;
+  p.sa_dev = sa_dev;
+  p.sb_dev = sb_dev;
+  p.sa = sa;
+  p.sb = sb;
+  p.col_scale = col_scale;
+  p.bias_f = bias;
+  return gemm_common(A, lda, a_layout, B, ldb, b_layout, M, N, K, p, 2, eco_stream(stream), "eco_gemm_s8_dequant");
 }
 
 extern "C" int eco_set_gemm_sm_limit(int max_ctas) {

@@ -104,6 +104,9 @@ _SIGS = {
     "eco_i8eco_step": (c_i32, [ctypes.POINTER(I8ECOLayer), c_i32, ctypes.POINTER(I8ECOHyper), c_p]),
     "eco_i8eco_finalize": (c_i32, [c_p, c_i32, c_p]),
     "eco_sgdm_step": (c_i32, [c_p, c_p, c_p, c_i64, c_i64, c_p, c_p, c_f, c_f, c_f, c_f, c_u64, c_p, c_p]),
+    "eco_gemm_s8_dequant": (c_i32, [c_p, c_i64, c_i32, c_p, c_i64, c_i32, c_i64, c_i64, c_i64, c_p, c_d, c_p, c_d,
+                                    c_p, c_p, c_p, c_i64, c_p]),
+    "eco_quantize_dynamic_f32": (c_i32, [c_p, c_i64, c_i64, c_i64, c_p, c_p, c_i64, c_p, c_p]),
     "eco_fp32_eco_step": (c_i32, [ctypes.POINTER(Fp32Layer), c_i32, ctypes.POINTER(Fp32Hyper), c_p, c_i64, c_p]),
     "eco_fp32_eco_scratch_len": (c_i64, [ctypes.POINTER(Fp32Layer), c_i32]),
 }

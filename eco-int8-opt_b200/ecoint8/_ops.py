@@ -62,6 +62,44 @@ def gemm_requant(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
     return y
 
 
+def gemm_dequant(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int, M: int, N: int, K: int,
+                 sa, sb, col_scale: torch.Tensor | None = None, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 ``[M, N] = fp32(A.B) * fp32(sa * sb) (* col_scale[n]) (+ bias[n])``; ``sa``/``sb`` are
+    Python floats or device scales (``_scale.DevScale``)."""
+    from . import _scale
+
+    nat.require_cuda(a, b, col_scale, bias)
+    a, lda = aligned(a)
+    b, ldb = aligned(b)
+    for t in (col_scale, bias):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != N):
+            raise RuntimeError("gemm_dequant: col_scale / bias must be contiguous fp32 of N values")
+    pa, va = _scale.gain_args(sa)
+    pb, vb = _scale.gain_args(sb)
+    y = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    nat.call("eco_gemm_s8_dequant", a.data_ptr(), lda, a_layout, b.data_ptr(), ldb, b_layout, M, N, K, pa, va, pb, vb,
+             nat.ptr(col_scale), nat.ptr(bias), y.data_ptr(), N, nat.stream())
+    return y
+
+
+def quantize_dynamic(x: torch.Tensor):
+    """``quantize_tensor_dynamic(x)`` (round to nearest) of a 2-D fp32 CUDA tensor with the
+    scale kept on the device: returns ``(int8 tensor, _scale.DevScale)``."""
+    from . import _scale
+
+    nat.require_cuda(x)
+    if x.dtype != torch.float32 or x.dim() != 2:
+        raise RuntimeError("quantize_dynamic: a 2-D fp32 tensor")
+    x = _rowmajor(x)
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), dtype=_I8, device=x.device)
+    amax = torch.empty(1, dtype=_I32, device=x.device)
+    scale = torch.empty(3, dtype=torch.int64, device=x.device)
+    nat.call("eco_quantize_dynamic_f32", x.data_ptr(), rows, cols, x.stride(0) if rows > 1 else cols,
+             amax.data_ptr(), q.data_ptr(), cols, scale.data_ptr(), nat.stream())
+    return q, _scale.DevScale(scale)
+
+
 def requant(src: torch.Tensor, mult, shift: int, site: Site, bias: torch.Tensor | None = None,
             relu: bool = False, mask: torch.Tensor | None = None,
             sumsq: torch.Tensor | None = None) -> torch.Tensor:

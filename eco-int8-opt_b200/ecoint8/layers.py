@@ -2,9 +2,8 @@
 
 ``Int8Linear`` keeps fp32 activations at its boundary (dynamic per-tensor
 quantization in, float dequantization out) and feeds fp32 weight gradients to
-``EcoInt8SGDM`` through ``layer._grad_w``.  Its three int8 GEMMs run on the
-B200 tcgen05 kernels (no padding); the float epilogues stay PyTorch, as in
-the reference (layers.py:45-75).
+the ECO optimizers through ``layer._grad_w``.  Its three int8 GEMMs run on the
+B200 tcgen05 kernels (no padding) with the fp32 epilogue fused (layers.py:45-75).
 """
 
 from __future__ import annotations
@@ -29,17 +28,24 @@ def _int_mm(a8: torch.Tensor, b8: torch.Tensor) -> torch.Tensor:
 
 
 class Int8LinearFunc(torch.autograd.Function):
-    """layers.py:45-75."""
+    """layers.py:45-75 with every int8 GEMM's fp32 epilogue fused into it and the dynamic
+    scales kept on the device (no ``.item()`` per call): the input and the output gradient
+    are quantized by ``eco_quantize_dynamic_f32`` (quant.py:35-38), and ``eco_gemm_s8_dequant``
+    computes ``acc.to(float32) * s_x * s_w.t() + bias``, ``dw_acc.float() * (s_g * s_x)`` and
+    ``dx_acc.float() * (s_g * s_w.mean())`` in PyTorch's fp32 operation order, bit for bit.
+    ``s_w.mean()`` is read once per layer (it is a frozen buffer) and cached."""
 
     @staticmethod
     def forward(ctx, x_f32, w_i8, s_w, bias, layer_ref):
-        x_i8, s_x = quantize_tensor_dynamic(x_f32)
-        acc = _int_mm(x_i8, w_i8.t())
-        y = acc.to(torch.float32) * s_x * s_w.t()
-        if bias is not None:
-            y = y + bias
+        if x_f32.dtype != torch.float32 or x_f32.dim() != 2:
+            raise RuntimeError("Int8Linear (B200 build): 2-D fp32 input")
+        x_i8, s_x = _ops.quantize_dynamic(x_f32)
+        M, K = x_i8.shape
+        N = w_i8.shape[0]
+        y = _ops.gemm_dequant(x_i8, 0, w_i8, 0, M, N, K, s_x, 1.0, col_scale=s_w.reshape(-1).contiguous(),
+                              bias=None if bias is None else bias.detach().contiguous())
         ctx.save_for_backward(x_i8, w_i8, s_w)
-        ctx.s_x = float(s_x)
+        ctx.s_x = s_x  # a device scale (the reference's float(s_x))
         ctx.has_bias = bias is not None
         ctx.layer_ref = layer_ref
         return y
@@ -47,18 +53,31 @@ class Int8LinearFunc(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         x_i8, w_i8, s_w = ctx.saved_tensors
-        s_x = ctx.s_x
-        g_i8, s_g = quantize_tensor_dynamic(grad_out)
+        g_i8, s_g = _ops.quantize_dynamic(grad_out.to(torch.float32))
         M, N = g_i8.shape
-        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, N, x_i8.shape[1], M)  # g^T x
-        grad_w = dw_acc.to(torch.float32) * (s_g * s_x)
-        dx_acc = _ops.gemm_s32(g_i8, 0, w_i8, 1, M, w_i8.shape[1], N)  # g w
-        grad_x = dx_acc.to(torch.float32) * (s_g * s_w.mean().item())
+        # dW: exact, both scales per-tensor (layers.py:63-64): g^T x
+        grad_w = _ops.gemm_dequant(g_i8, 1, x_i8, 1, N, x_i8.shape[1], M, s_g, ctx.s_x)
+        # dX: the per-channel s_w replaced by its mean (:66-67): g w
+        grad_x = _ops.gemm_dequant(g_i8, 0, w_i8, 1, M, w_i8.shape[1], N, s_g, _sw_mean(s_w))
         grad_bias = grad_out.sum(0) if ctx.has_bias else None
         layer = ctx.layer_ref()
         if layer is not None:
             layer._grad_w = grad_w
         return grad_x, None, None, grad_bias, None
+
+
+_SW_MEAN: dict = {}  # (storage, version) -> float(s_w.mean())
+
+
+def _sw_mean(s_w: torch.Tensor) -> float:
+    """``s_w.mean().item()`` (PyTorch's own fp32 reduction), cached while the buffer is unchanged."""
+    key = (s_w.data_ptr(), s_w._version, s_w.numel())
+    v = _SW_MEAN.get(key)
+    if v is None:
+        if len(_SW_MEAN) > 4096:
+            _SW_MEAN.clear()
+        v = _SW_MEAN[key] = s_w.mean().item()
+    return v
 
 
 class Int8Linear(nn.Module):

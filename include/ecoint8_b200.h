@@ -133,6 +133,19 @@ ECO_API int eco_gemm_s8_requant(const int8_t* A, int64_t lda, int a_layout, cons
                         const int32_t* mult, int shift, int relu, eco_sr_t sr, int8_t* Y,
                         int64_t ldy, eco_stream_t stream);
 
+/* Int8LinearFunc's GEMMs with their fp32 epilogue fused (layers.py:45-75):
+ * Y[m, n] = fp32(C[m, n]) * fp32(sa * sb), then * col_scale[n] (nullable), then
+ * + bias[n] (nullable), each one IEEE fp32 operation like PyTorch's kernels; C = A.B as in
+ * eco_gemm_s8s32 (int32, never stored).  sa / sb: doubles, each read from the device
+ * (double bits at sa_dev / sb_dev, e.g. a scale from eco_quantize_dynamic_f32) when the
+ * pointer is given, else the host value.  Replaces _int_mm + `acc.to(float32) * s_x *
+ * s_w.t() + bias` (:48-52) and `dw_acc.float() * (s_g * s_x)`, `dx_acc.float() * (s_g *
+ * s_w.mean())` (:63-67). */
+ECO_API int eco_gemm_s8_dequant(const int8_t* A, int64_t lda, int a_layout, const int8_t* B, int64_t ldb,
+                                int b_layout, int64_t M, int64_t N, int64_t K, const int64_t* sa_dev, double sa,
+                                const int64_t* sb_dev, double sb, const float* col_scale, const float* bias,
+                                float* Y, int64_t ldy, eco_stream_t stream);
+
 /* ---------------------------------------------------------- elementwise --
  * dst = sat8(SR((src + bias[c]) * m, shift)), m = mult_col[c] or mult_scalar;
  * then dst = 0 where mask[r,c] <= 0 (mask nullable); relu clamps at 0;
@@ -154,6 +167,14 @@ ECO_API int eco_apply_mult_shift(const void* x, int x_bits, int64_t rows, int64_
 /* out[c] = sum_r g[r, c] (int64).  Replaces ilayer.py:168 (g.int32.sum(0)). */
 ECO_API int eco_colsum_s8(const int8_t* g, int64_t rows, int64_t cols, int64_t ld, int64_t* out,
                   eco_stream_t stream);
+
+/* quantize_tensor_dynamic (quant.py:35-38, stochastic=False) of an fp32 [rows, cols]
+ * matrix without a host round trip: *amax (overwritten) = the bits of max |x|;
+ * s = calc_scale(max |x|) (quant.py:9-16) in double; q = clamp(round(x / (s + 1e-8)),
+ * +-127) with PyTorch's CUDA arithmetic (a multiply by the fp32 reciprocal of the
+ * scalar, round half to even).  scale_out: int64[3] = {double bits of s, 0, 0}. */
+ECO_API int eco_quantize_dynamic_f32(const float* x, int64_t rows, int64_t cols, int64_t ld, int32_t* amax,
+                                     int8_t* q, int64_t ld_q, int64_t* scale_out, eco_stream_t stream);
 
 /* *out = max |x| over n int32/int64 elements (device int64 word, overwritten).
  * Replaces fixedpoint.int_amax's reduction (fixedpoint.py:85-88). */

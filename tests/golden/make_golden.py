@@ -402,6 +402,35 @@ def gen_fp32_eco(ref):
     return cases
 
 
+INT8_LINEAR_CASES = [(64, 40, 24, True, 21), (33, 70, 17, False, 22), (8, 16, 8, True, 23)]  # N, in, out, bias, seed
+
+
+def int8_linear_inputs(layer_cls, n, in_f, out_f, bias, seed, torch):
+    torch.manual_seed(seed)
+    layer = layer_cls(in_f, out_f, bias)
+    if bias:
+        layer.bias.data.copy_(torch.randn(out_f) * 0.1)
+    x = torch.randn(n, in_f) * 2.0
+    gy = torch.randn(n, out_f) * 0.05
+    return layer, x, gy
+
+
+def gen_int8_linear(ref):
+    """Int8Linear forward and backward through autograd (layers.py:45-111) on CPU."""
+    import torch
+
+    cases = []
+    for n, in_f, out_f, bias, seed in INT8_LINEAR_CASES:
+        layer, x, gy = int8_linear_inputs(ref["Int8Linear"], n, in_f, out_f, bias, seed, torch)
+        x.requires_grad_(True)
+        y = layer(x)
+        y.backward(gy)
+        cases.append({"n": n, "in": in_f, "out": out_f, "bias": bias, "seed": seed, "w": digest(layer.w_i8),
+                      "y": digest(y.detach()), "grad_x": digest(x.grad), "grad_w": digest(layer._grad_w),
+                      "grad_bias": digest(layer.bias.grad) if bias else None})
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ECOINT8_REFERENCE"),
@@ -439,6 +468,7 @@ def main():
         "sgdm_triton.json": lambda: gen_sgdm_triton(ref),
         "wide_train.json": lambda: gen_wide(ref, bnd, 2),
         "fp32_eco.json": lambda: gen_fp32_eco(ref),
+        "int8_linear.json": lambda: gen_int8_linear(ref),
     }
     if args.only:
         torch.set_num_threads(os.cpu_count() or 1)  # the wide fixture's GEMMs (results do not depend on it)

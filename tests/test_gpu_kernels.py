@@ -197,22 +197,28 @@ def test_peer_push_signal_and_bounded_wait_on_one_gpu():
     fl = (ctypes.c_void_p * 1)(flags.data_ptr())
     torch.cuda.synchronize()
     assert _native.read_device_errors() == 0
-    _native.call("eco_peer_signal", fl, 1, 0, 2, 7, s)
-    _native.call("eco_peer_wait", flags.data_ptr(), 1, 2, 7, 100000, s)
+    _native.call("eco_peer_signal", fl, 1, 0, 2, 7, None, s)
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 2, 7, None, 100000, s)
     torch.cuda.synchronize()
     assert int(flags[2, 0]) == 7 and _native.read_device_errors() == 0
+    # epochs read from device memory when the kernels run (as a replayed CUDA graph does)
+    word = torch.tensor([9], dtype=torch.int64, device="cuda")
+    _native.call("eco_peer_signal", fl, 1, 0, 2, 0, word.data_ptr(), s)
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 2, 0, word.data_ptr(), 100000, s)
+    torch.cuda.synchronize()
+    assert int(flags[2, 0]) == 9 and _native.read_device_errors() == 0
     # push and signal in one launch (every CTA fenced first); the ticket returns to zero
     src = torch.randint(-127, 128, (300, 64), dtype=torch.int8, generator=gen).cuda()
     dst = torch.zeros((300, 64), dtype=torch.int8, device="cuda")
     ticket = torch.zeros(1, dtype=torch.int32, device="cuda")
     arr = (ctypes.c_void_p * 1)(dst.data_ptr())
-    _native.call("eco_peer_push_signal_s8", src.data_ptr(), 64, 300, 64, arr, 1, 64, 0, 0, 7, fl, 1, 0, 1, 3,
+    _native.call("eco_peer_push_signal_s8", src.data_ptr(), 64, 300, 64, arr, 1, 64, 0, 0, 7, fl, 1, 0, 1, 3, None,
                  ticket.data_ptr(), s)
-    _native.call("eco_peer_wait", flags.data_ptr(), 1, 1, 3, 100000, s)
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 1, 3, None, 100000, s)
     torch.cuda.synchronize()
     assert torch.equal(dst, src) and int(flags[1, 0]) == 3 and int(ticket) == 0
     assert _native.read_device_errors() == 0
-    _native.call("eco_peer_wait", flags.data_ptr(), 1, 3, 1, 100000, s)  # nothing signals slot 3
+    _native.call("eco_peer_wait", flags.data_ptr(), 1, 3, 1, None, 100000, s)  # nothing signals slot 3
     torch.cuda.synchronize()
     assert _native.read_device_errors() == 4
     assert _native.read_device_errors() == 0  # the read clears the flags

@@ -325,3 +325,21 @@ def test_fp32_eco_oracle_matches_reference_golden(golden):
             if c["kind"] == "adam":
                 assert [digest(vv) for vv in v] == want["v"]
             assert float(tot / n_e).hex() == want["mean_abs_e"]
+
+
+def test_int8_linear_oracle_matches_reference_golden(golden):
+    """The op-by-op PyTorch restatement of Int8LinearFunc (oracle/float_layers.py) against the
+    reference's Int8Linear run through autograd on CPU: bit-exact output and gradients."""
+    import torch
+
+    from ecoint8.layers import Int8Linear
+    from oracle import float_layers as fl
+    from tests.golden.make_golden import digest, int8_linear_inputs
+
+    for c in golden("int8_linear.json"):
+        layer, x, gy = int8_linear_inputs(Int8Linear, c["n"], c["in"], c["out"], c["bias"], c["seed"], torch)
+        assert digest(layer.w_i8) == c["w"]
+        y, x_i8, s_x = fl.forward(x, layer.w_i8, layer.s_w, layer.bias.detach() if c["bias"] else None)
+        gx, gw, gb = fl.backward(gy, x_i8, layer.w_i8, layer.s_w, s_x, c["bias"])
+        assert digest(y) == c["y"] and digest(gx) == c["grad_x"] and digest(gw) == c["grad_w"]
+        assert (digest(gb) if c["bias"] else None) == c["grad_bias"]
