@@ -27,6 +27,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "abi.cuh"
 #include "common.cuh"
@@ -487,6 +488,254 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------ CTA-pair kernel
+// The same GEMM with 256 x 256 output tiles computed by a cluster of two CTAs on
+// neighbouring SMs (tcgen05 cta_group::2).  CTA r of the pair loads rows [128 r, 128 r +
+// 128) of the A tile and columns [128 r, 128 r + 128) of the B tile into its own shared
+// memory (no multicast: every TMA load fills only the issuing CTA's memory); the even
+// CTA issues tcgen05.mma.cta_group::2 (M = 256, N = 256), which reads both CTAs' halves
+// and leaves each CTA's 128 rows of the accumulator in that CTA's TMEM.  Per SM and
+// K slice this moves 32 KB from L2 instead of 48 KB.  Barriers: both CTAs' loads
+// complete on the even CTA's `full` barrier (cp.async.bulk.tensor .cta_group::2); the
+// MMA's commits arrive on both CTAs' `empty` / `tfull` barriers (multicast commit);
+// both CTAs' epilogue warps arrive on the even CTA's `tempty` barrier.  Every wait is
+// bounded as in the one-CTA kernel; both CTAs meet at cluster barriers after the
+// barrier setup and before TMEM is freed (the even CTA's MMAs read the odd CTA's memory).
+constexpr int PBN = 256;                         // tile N (both CTAs)
+constexpr int PHALF_B = (PBN / 2) * BK;          // B bytes per CTA and stage
+constexpr int PS = 6;                            // stages
+constexpr int PSMEM = PS * (BM * BK + PHALF_B) + 1024 + 1024;
+
+ECO_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+ECO_DEV uint32_t map_to_rank0(const void* p) {  // the same shared variable in CTA 0 of the cluster
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+  return r;
+}
+ECO_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+ECO_DEV void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+ECO_DEV void umma_s8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+ECO_DEV void umma_commit_pair(uint64_t* bar) {  // arrive on `bar` in both CTAs of the pair
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+ECO_DEV void umma_commit_pair_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+ECO_DEV void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+// Instruction descriptor of the pair MMA: as idesc_s8 with M = 256.
+ECO_DEV uint32_t idesc_s8_pair(int n, int a_mn, int b_mn) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_s8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmParams p) {
+  constexpr int S = PS;
+  constexpr int A_BYTES = BM * BK, B_BYTES = PHALF_B;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * B_BYTES);  // used in CTA 0: both CTAs' bytes
+  uint64_t* empty = full + S;                                        // each CTA: its stage is free
+  uint64_t* tfull = empty + S;                                       // each CTA: accumulator ready
+  uint64_t* tempty = tfull + 2;                                      // CTA 0: both CTAs drained it
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (warp == 0 && lane == 0) {
+    *abort_flag = 0u;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * PBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before either CTA signals the other's
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += n_pairs) {
+        int mb, nb;
+        tile_coords(p, t, mb, nb);
+        const int m0 = mb * 2 * BM + (int)rank * BM, n0 = nb * PBN + (int)rank * (PBN / 2);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&empty[s], ((uint32_t)(it / S) & 1u) ^ 1u)) {
+            *abort_flag = 1u;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (A_BYTES + B_BYTES));
+          const uint32_t bar = map_to_rank0(&full[s]);
+          const int k0 = kb * BK;
+          uint8_t* a_dst = sA + s * A_BYTES;
+          uint8_t* b_dst = sB + s * B_BYTES;
+          if (p.a_mn)
+            tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
+          else
+            tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+          if (p.b_mn)
+            tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
+          else
+            tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
+        }
+      }
+      // drain: the MMAs released (consumed) the last stages this CTA filled
+      for (int k = it > S ? it - S : 0; k < it; ++k) mbar_wait(&empty[k % S], (uint32_t)(k / S) & 1u);
+    }
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = idesc_s8_pair(PBN, p.a_mn, p.b_mn);
+      const uint32_t a_kstep = p.a_mn ? 32 * 128 : 32, b_kstep = p.b_mn ? 32 * 128 : 32;
+      const uint32_t a_lbo = p.a_mn ? 128 * BK : 16, b_lbo = p.b_mn ? 128 * BK : 16;
+      int it = 0, j = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += n_pairs, ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&tempty[b], ((uint32_t)(j >> 1) & 1u) ^ 1u)) {
+          *abort_flag = 1u;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + (uint32_t)(b * PBN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (uint32_t)(it / S) & 1u)) {
+            *abort_flag = 1u;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + s * A_BYTES), b_base = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            umma_s8_pair(d_tmem, smem_desc(a_base + kk * a_kstep, a_lbo, 1024),
+                         smem_desc(b_base + kk * b_kstep, b_lbo, 1024), idesc, (kb | kk) != 0);
+          umma_commit_pair(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[b]);
+      }
+      umma_commit_pair_local(drain);  // arrives once every MMA issued above has retired
+      mbar_wait(drain, 0);
+    }
+  } else {
+    const int e = warp - 2;
+    const int q = warp & 3;
+    const int half = e >> 2;
+    constexpr int kChunks = PBN / 64;
+    PhiloxKeys keys;
+    const eco_sr_t sr = sr_resolve(p.sr, p.keys, keys);
+    float scalar = 0.0f;
+    if (EPI == 2) {
+      const double a = p.sa_dev ? __longlong_as_double(*p.sa_dev) : p.sa;
+      const double b = p.sb_dev ? __longlong_as_double(*p.sb_dev) : p.sb;
+      scalar = __double2float_rn(__dmul_rn(a, b));
+    }
+    const uint32_t tempty0 = map_to_rank0(&tempty[0]), tempty1 = map_to_rank0(&tempty[1]);
+    i64 amax = 0;
+    int j = 0;
+    for (int t = pair; t < num_tiles; t += n_pairs, ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&tfull[b], (uint32_t)(j >> 1) & 1u) || *abort_flag) {
+        *abort_flag = 1u;
+        break;
+      }
+      tc_fence_after();
+      int mb, nb_t;
+      tile_coords(p, t, mb, nb_t);
+      const int m = mb * 2 * BM + (int)rank * BM + q * 32 + lane;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        const int col = half * (PBN / 2) + c * 32;
+        const int nb = nb_t * PBN + col;
+        uint32_t v[32];
+        tmem_ld32(tmem + (uint32_t)(b * PBN + col) + ((uint32_t)(q * 32) << 16), v);
+        if (nb >= p.N) continue;  // warp-uniform
+        const int n_lane = nb + lane;
+        if (EPI == 2) {
+          const float cs = (p.col_scale && n_lane < p.N) ? __ldg(p.col_scale + n_lane) : 0.0f;
+          const float bf = (p.bias_f && n_lane < p.N) ? __ldg(p.bias_f + n_lane) : 0.0f;
+          epi_store_dequant(p, scalar, v, m, nb, cs, bf);
+          continue;
+        }
+        const int bias_lane = (p.bias && n_lane < p.N) ? __ldg(p.bias + n_lane) : 0;
+        if (EPI == 0) {
+          epi_store_s32(p, v, m, nb, bias_lane, amax);
+        } else {
+          const int mult_lane = n_lane < p.N ? __ldg(p.mult + n_lane) : 0;
+          epi_store_requant(p, sr, keys, v, m, nb, bias_lane, mult_lane);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(b ? tempty1 : tempty0);
+    }
+    if (EPI == 0 && p.amax) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = max(amax, (i64)__shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0 && amax > 0) atomicMax(p.amax, (int)amax);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the even CTA's MMAs are done with the odd CTA's memory
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * PBN));
+  }
+}
+
 // ------------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -543,6 +792,48 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   return eco_launch_check("gemm_s8_kernel");
 }
 
+// CTA pairs for the large GEMMs: on when ECO_GEMM_PAIRS=1 in the environment (read once).
+bool pairs_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("ECO_GEMM_PAIRS");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+template <int EPI>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+  auto kern = gemm_s8_pair_kernel<EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PSMEM) != cudaSuccess)
+      return eco_launch_check("gemm (pairs): cudaFuncSetAttribute");
+    attr_set = true;
+  }
+  GemmParams q = p;
+  q.tiles_m = (p.M + 2 * BM - 1) / (2 * BM);
+  q.tiles_n = (p.N + PBN - 1) / PBN;
+  const int tiles = q.tiles_m * q.tiles_n;
+  int ctas = eco_num_sms();
+  if (g_gemm_sm_limit > 0) ctas = std::min(ctas, g_gemm_sm_limit);
+  const int pairs = std::max(1, std::min(tiles, ctas / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = PSMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, q) != cudaSuccess) return eco_launch_check("gemm_s8_pair_kernel launch");
+  return eco_launch_check("gemm_s8_pair_kernel");
+}
+
 int gemm_common(const int8_t* A, i64 lda, int a_layout, const int8_t* B, i64 ldb, int b_layout, i64 M, i64 N, i64 K,
                 GemmParams& p, int epi, cudaStream_t s, const char* who) {
   ECO_REQUIRE(A && B && M > 0 && N > 0 && K > 0, ECO_ERR_ARG, "%s: null operand or empty shape", who);
@@ -558,7 +849,15 @@ int gemm_common(const int8_t* A, i64 lda, int a_layout, const int8_t* B, i64 ldb
   p.a_mn = a_layout;
   p.b_mn = b_layout;
   const int BN = N <= 128 ? 128 : 256;
+  const bool pair = BN == 256 && M > BM && pairs_enabled() &&
+                    (g_gemm_sm_limit == 0 || g_gemm_sm_limit >= 2) && eco_num_sms() >= 2;
   CUtensorMap ta, tb;
+  if (pair) {  // each CTA of a pair loads a 128-row box of A and a 128-column box of B
+    if (int rc = a_layout ? make_tmap(&ta, A, M, K, lda, 128, BK) : make_tmap(&ta, A, K, M, lda, BK, BM)) return rc;
+    if (int rc = b_layout ? make_tmap(&tb, B, N, K, ldb, 128, BK) : make_tmap(&tb, B, K, N, ldb, BK, PBN / 2))
+      return rc;
+    return epi == 2 ? launch_pair<2>(ta, tb, p, s) : epi ? launch_pair<1>(ta, tb, p, s) : launch_pair<0>(ta, tb, p, s);
+  }
   if (int rc = a_layout ? make_tmap(&ta, A, M, K, lda, 128, BK) : make_tmap(&ta, A, K, M, lda, BK, BM)) return rc;
   if (int rc = b_layout ? make_tmap(&tb, B, N, K, ldb, 128, BK) : make_tmap(&tb, B, K, N, ldb, BK, BN)) return rc;
   if (BN == 128)

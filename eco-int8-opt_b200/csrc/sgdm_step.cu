@@ -8,6 +8,12 @@
 // (no fused multiply-add).  The two divisions by 127 of the host glue follow
 // PyTorch's CUDA kernel for a tensor divided by a Python scalar: a multiply
 // by the fp32 reciprocal 1/127.
+//
+// Work per element: the reference draws five Philox4x32-10 words per element (two in
+// pass 1, three in pass 2, each from its own counter), so the passes are bound by the
+// integer issue rate, not by HBM.  The round keys are expanded once per launch (host)
+// and kept in registers; threads walk the elements with an incremental (row, column)
+// so no division by the row length is done per element.
 #include <algorithm>
 
 #include "abi.cuh"
@@ -27,6 +33,38 @@ struct SgdmArgs {
   float lr, beta, wd, alpha;
   u64 seed;
   uint32_t* scratch;
+  PhiloxKeys keys;  // round keys of seed
+};
+
+// Triton's tl.rand(seed, offset) (common.cuh: tl_rand) with the round keys given.
+ECO_DEV float tl_rand_k(const PhiloxKeys& K, uint32_t offset) {
+  const Philox4 o = philox10k(offset, 0u, 0u, 0u, K);
+  int x = (int)o.x;
+  x = x < 0 ? -x - 1 : x;
+  return __fmul_rn(__int2float_rn(x), 4.6566127342e-10f);
+}
+
+// Element walk: thread t starts at element i0 = blockIdx.x * blockDim.x + t and steps by
+// the grid size; (r, c) of the element are advanced without a division per step.
+struct Walk {
+  i64 i, r, c, step, dr, dc;
+  ECO_DEV Walk(const SgdmArgs& a) {
+    i = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+    step = (i64)gridDim.x * blockDim.x;
+    r = i / a.cols;
+    c = i - r * a.cols;
+    dr = step / a.cols;
+    dc = step - dr * a.cols;
+  }
+  ECO_DEV void next(i64 cols) {
+    i += step;
+    r += dr;
+    c += dc;
+    if (c >= cols) {
+      c -= cols;
+      ++r;
+    }
+  }
 };
 
 ECO_DEV float inv127() { return __fdiv_rn(1.0f, 127.0f); }
@@ -72,12 +110,13 @@ ECO_DEV float sg_of(const SgdmArgs& a) {
 
 __global__ void __launch_bounds__(kThreads) pass1_kernel(const SgdmArgs a) {
   const float sg = sg_of(a), sm = *a.sm;
+  const PhiloxKeys K = a.keys;
   float v = 0.0f;
-  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += (i64)gridDim.x * blockDim.x) {
-    const uint32_t b = (uint32_t)((u64)i * 2u);
+  for (Walk t(a); t.i < a.n; t.next(a.cols)) {
+    const uint32_t b = (uint32_t)((u64)t.i * 2u);
     float wq, m_new;
-    eco_elem((float)a.w[i], (float)a.m[i], a.g[i], a.sw[i / a.cols], sm, sg, a, tl_rand(a.seed, b),
-             tl_rand(a.seed, b + 1u), wq, m_new);
+    eco_elem((float)a.w[t.i], (float)a.m[t.i], a.g[t.i], a.sw[t.r], sm, sg, a, tl_rand_k(K, b), tl_rand_k(K, b + 1u),
+             wq, m_new);
     v = fmaxf(v, fabsf(m_new));
   }
   block_max_to(v, &a.scratch[1]);
@@ -88,14 +127,15 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const SgdmArgs a) {
   const float sg = sg_of(a), sm = *a.sm;
   const float sm_new = __fmul_rn(__uint_as_float(a.scratch[1]), inv127());
   const float smg = __fadd_rn(sm_new, 1e-8f);
-  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < a.n; i += (i64)gridDim.x * blockDim.x) {
-    const uint32_t b = (uint32_t)((u64)i * 3u);
+  const PhiloxKeys K = a.keys;
+  for (Walk t(a); t.i < a.n; t.next(a.cols)) {
+    const uint32_t b = (uint32_t)((u64)t.i * 3u);
     float wq, m_new;
-    eco_elem((float)a.w[i], (float)a.m[i], a.g[i], a.sw[i / a.cols], sm, sg, a, tl_rand(a.seed, b),
-             tl_rand(a.seed, b + 1u), wq, m_new);
-    const float mq = fminf(fmaxf(floorf(__fadd_rn(__fdiv_rn(m_new, smg), tl_rand(a.seed, b + 2u))), -127.0f), 127.0f);
-    a.w[i] = (int8_t)wq;
-    a.m[i] = (int8_t)mq;
+    eco_elem((float)a.w[t.i], (float)a.m[t.i], a.g[t.i], a.sw[t.r], sm, sg, a, tl_rand_k(K, b), tl_rand_k(K, b + 1u),
+             wq, m_new);
+    const float mq = fminf(fmaxf(floorf(__fadd_rn(__fdiv_rn(m_new, smg), tl_rand_k(K, b + 2u))), -127.0f), 127.0f);
+    a.w[t.i] = (int8_t)wq;
+    a.m[t.i] = (int8_t)mq;
   }
   __threadfence();
   __syncthreads();
@@ -117,7 +157,7 @@ extern "C" int eco_sgdm_step(int8_t* w, int8_t* m, const float* g, int64_t rows,
   ECO_REQUIRE(w && m && g && sw && sm && scratch && rows > 0 && cols > 0, ECO_ERR_ARG,
               "eco_sgdm_step: bad arguments");
   ECO_REQUIRE(rows * cols < (1ll << 31), ECO_ERR_ARG, "eco_sgdm_step: layer exceeds int32 element offsets");
-  SgdmArgs a{w, m, g, rows * cols, cols, sw, sm, lr, beta, wd, alpha, seed, scratch};
+  SgdmArgs a{w, m, g, rows * cols, cols, sw, sm, lr, beta, wd, alpha, seed, scratch, philox_keys(seed)};
   cudaStream_t s = eco_stream(stream);
   if (cudaMemsetAsync(scratch, 0, 4 * sizeof(uint32_t), s) != cudaSuccess) return eco_launch_check("eco_sgdm_step memset");
   const i64 cap = (i64)eco_num_sms() * 8;
