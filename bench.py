@@ -796,8 +796,10 @@ def main():
             out["requant"] = requant_measurement(device)
             achieved = ops / times["dx"] / 1e12
             out["roofline"] = {"bound": "tensor",
-                               "kernel": "gemm_s8_kernel<256,0> (int32 + max|C|, the dX GEMM: 16384x8192x8192, "
-                                         "B MN-major; 26 of the step's GEMM launches are this kernel)",
+                               "kernel": ("gemm_s8_pair_kernel<0>" if os.environ.get("ECO_GEMM_PAIRS", "1") != "0"
+                                          else "gemm_s8_kernel<256,0>")
+                                         + " (int32 + max|C|, the dX GEMM: 16384x8192x8192, B MN-major; "
+                                           "the step's dX and dW GEMMs are this kernel)",
                                "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                                "peak_source": f"measured int8 dense peak on this GPU: best of {peak_where} "
                                               f"(2 x {src} bf16 = {2 * bf16:.0f} for context)",

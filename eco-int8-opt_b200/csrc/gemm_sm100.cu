@@ -792,12 +792,13 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   return eco_launch_check("gemm_s8_kernel");
 }
 
-// CTA pairs for the large GEMMs: on when ECO_GEMM_PAIRS=1 in the environment (read once).
+// CTA pairs for the large GEMMs: on unless ECO_GEMM_PAIRS=0 in the environment (read once;
+// the one-CTA kernel then runs every shape).
 bool pairs_enabled() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("ECO_GEMM_PAIRS");
-    v = (e && e[0] == '1') ? 1 : 0;
+    v = (e && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
 }

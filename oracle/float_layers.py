@@ -29,22 +29,16 @@ def quantize_tensor_dynamic(x: torch.Tensor):
     return torch.clamp(torch.round(v), -127, 127).to(torch.int8), s
 
 
-def _pad8(v: int) -> int:
-    return (v + 7) // 8 * 8
-
-
 def int_mm(a8: torch.Tensor, b8: torch.Tensor) -> torch.Tensor:
-    """layers.py:26-42 (``pad_mm_dims``: M to at least 32 and a multiple of 8, K and N to 8)."""
+    """layers.py:26-42: the exact int8 x int8 -> int32 product.  On CPU it is the reference's
+    ``torch._int_mm``; on CUDA the reference pads (``pad_mm_dims``) and calls cuBLASLt, which
+    rejects some padded shapes (e.g. M 33, K 17, N 70), so here the product is taken in float64
+    on the device -- exact, like every int8 GEMM, since each partial sum is an integer far
+    below 2^53 -- and the int32 result is the same."""
     a8 = a8.contiguous()
     b8 = b8.contiguous()
     if a8.is_cuda:
-        M, K = a8.shape
-        N = b8.shape[1]
-        M8, K8, N8 = max(32, _pad8(M)), _pad8(K), _pad8(N)
-        if (M8, K8, N8) != (M, K, N):
-            a8 = torch.nn.functional.pad(a8, (0, K8 - K, 0, M8 - M))
-            b8 = torch.nn.functional.pad(b8, (0, N8 - N, 0, K8 - K))
-            return torch._int_mm(a8, b8)[:M, :N]
+        return (a8.to(torch.float64) @ b8.to(torch.float64)).to(torch.int32)
     return torch._int_mm(a8, b8)
 
 
