@@ -803,7 +803,7 @@ def main():
                                "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                                "peak_source": f"measured int8 dense peak on this GPU: best of {peak_where} "
                                               f"(2 x {src} bf16 = {2 * bf16:.0f} for context)",
-                               "frac": achieved / peak, "traffic": _traffic("gemm_s32_dx_16384x8192x8192.md"),
+                               "frac": achieved / peak, "traffic": _traffic("gemm_pair_dx_16384x8192x8192.md"),
                                "dw": {"achieved": ops / times["dw"] / 1e12, "frac": ops / times["dw"] / 1e12 / peak,
                                       "shape": "8192x8192 over batch 16384, A and B MN-major"},
                                "fused_forward": {"achieved": ops / times["fused"] / 1e12,
