@@ -21,7 +21,8 @@
 // of S is this kernel's own (lane-sequential, then a butterfly), so g agrees
 // with PyTorch's CUDA cross-entropy gradient to within a few ulp; the
 // quantization of a given g is PyTorch's own arithmetic bit for bit (division
-// by the Python scalar s_g + EPS as a multiply by its fp32 reciprocal).
+// by the Python scalar s_g + EPS as a multiply by its reciprocal, taken in double
+// and rounded to fp32).
 #include <algorithm>
 
 #include "abi.cuh"
@@ -106,7 +107,8 @@ struct QuantArgs {
 };
 
 // s_g = calc_scale(max|g|) in double (quant.py:9-16), then PyTorch's division of an
-// fp32 tensor by the Python scalar s_g + EPS: a multiply by its fp32 reciprocal.
+// fp32 tensor by the Python scalar s_g + EPS: a multiply by its reciprocal, taken in
+// double and rounded to fp32.
 ECO_DEV double scale_of(const QuantArgs& A) {
   const uint32_t bits = A.amax_bits == 32 ? (uint32_t) * static_cast<const int32_t*>(A.amax)
                                           : (uint32_t) * static_cast<const int64_t*>(A.amax);
@@ -136,7 +138,7 @@ __global__ void ce_quantize_kernel(const __grid_constant__ QuantArgs A) {
     if (threadIdx.x == 0) A.loss_out[0] = __fdiv_rn(part[0], (float)A.count);
   }
   if (r >= A.rows) return;
-  const float inv = __fdiv_rn(1.0f, __double2float_rn(__dadd_rn(s_g, 1e-8)));
+  const float inv = __double2float_rn(__ddiv_rn(1.0, __dadd_rn(s_g, 1e-8)));
   const int8_t* row = A.L + r * A.ld;
   const float2 st = A.stats[r];
   const int64_t y = A.labels[r];

@@ -181,6 +181,23 @@ ECO_DEV void eco_elem_fast(const FastRow& c, int w, int m, int g, int nw, int& m
   m_new_out = m_new;
 }
 
+// Four int32 saturated to [-127, 127] and packed into bytes (a lowest): two saturating
+// pack conversions (to [-128, 127]) and one per-byte max with -127.
+ECO_DEV uint32_t pack4_sat127(int a, int b, int c, int d) {
+  uint32_t hi, r;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(d), "r"(c));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  return __vmaxs4(r, 0x81818181u);
+}
+
+// Four int32 in [-128, 127] packed into bytes (a lowest): two pack conversions.
+ECO_DEV uint32_t pack4_cvt(int a, int b, int c, int d) {
+  uint32_t hi, r;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(d), "r"(c));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  return r;
+}
+
 // (x >> s) as int32 (the result fits): the high word shifted when s >= 32 (HI),
 // else one funnel shift.
 template <bool HI>
@@ -199,7 +216,7 @@ ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 st
                        int8_t* mr, const int8_t* gr, int nch, int lane, u64& rsum) {
   const int mmu = (int)c.mult_m, mgu = (int)c.mult_g, mmm = (int)c.mult_mm;
   const i64 hm = c.half_m, hg = c.half_g;
-  const int cm = c.com_m, cg = c.com_g, lo = c.com_mm - 20, shm = c.com_mm - 32;
+  const int cm = c.com_m, cg = c.com_g, lo = c.com_mm - 20, shm = c.com_mm - 32, lo12 = lo - 12;
   const uint32_t p2lo = 1u << lo;
   const int bq = (int)c.b_q, nbq = (int)c.nb_q, lrq = (int)c.lr_q, aq = (int)c.a_q;
   int rmx = 0, rmn = 0;
@@ -221,12 +238,12 @@ ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 st
     const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mv);
     const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv);
     uint32_t wo[4], mo[4];
-    int rsum32 = 0;
+    unsigned rsum32 = 0u;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const Philox4 rnd = sr_quad_k(keys, stream, row, (uint32_t)(4 * j + q));
-      int wq[4], mq[4];
-      unsigned ties = 0u;
+      int wq[4], mq[4], mn[4];
+      uint32_t tf[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t f = quad_word(rnd, k);
@@ -238,33 +255,30 @@ ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 st
         const int wn = max(min((thU + (int)(f & 0xFFFu)) >> 12, 127), -127);
         const int eU = thU - wn * 4096;
         const int m_new = m_t + shr_fit(mul_wide_s32(eU, aq), 16);
-        rmx = max(rmx, m_new);
-        rmn = min(rmn, m_new);
-        rsum32 += abs(eU);
+        mn[k] = m_new;
+        rsum32 = __sad(eU, 0, rsum32);
         const i64 p2 = mad_wide_u32(f >> 12, p2lo, mul_wide_s32(m_new, mmm));
-        // the tie-break draw matters only when bits [lo, lo + 20) of p2 are all ones
-        ties |= (unsigned)((__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) & 0xFFFFFu) == 0xFFFFFu) << k;
+        // the tie-break draw matters only when bits [lo, lo + 20) of p2 are all ones;
+        // they are the top 20 bits of tf
+        tf[k] = __funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo12);
         wq[k] = wn;
-        mq[k] = max(min(hi32(p2) >> shm, 127), -127);
+        mq[k] = hi32(p2) >> shm;
       }
-      if (ties) {  // rare (2^-20 per element): redo the tied elements with the exact draw
+      rmx = __vimax3_s32(rmx, __vimax3_s32(mn[0], mn[1], mn[2]), mn[3]);
+      rmn = __vimin3_s32(rmn, __vimin3_s32(mn[0], mn[1], mn[2]), mn[3]);
+      if (__vimax3_u32(__vimax3_u32(tf[0], tf[1], tf[2]), tf[3], 0u) >= 0xFFFFF000u) {
+        // rare (2^-20 per element): the tied elements take the exact draw
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          if (!((ties >> k) & 1u)) continue;
-          const uint32_t f = quad_word(rnd, k);  // the element again, from its inputs
-          const int mU = shr_sel<HM>(mad_wide_s32(sbyte(mw[q], k), mmu, hm), cm);
-          const int gU = shr_sel<HG>(mad_wide_s32(sbyte(gw[q], k), mgu, hg), cg);
-          const int m_t = shr_fit(mad_wide_s32(gU, nbq, mul_wide_s32(mU, bq)), 16);
-          const int thU = sbyte(ww[q], k) * 4096 - shr_fit(mul_wide_s32(m_t, lrq), 16);
-          const int eU = thU - wq[k] * 4096;
-          const int m_new = m_t + shr_fit(mul_wide_s32(eU, aq), 16);
-          const i64 p2 = mad_wide_u32(f >> 12, p2lo, mul_wide_s32(m_new, mmm));
-          mq[k] = (int)max((i64)-127, min((i64)127, step_m_round_tie(p2, c.com_mm, seed, stream, row,
+          if (tf[k] < 0xFFFFF000u) continue;
+          const uint32_t f = quad_word(rnd, k);
+          const i64 p2 = mad_wide_u32(f >> 12, p2lo, mul_wide_s32(mn[k], mmm));
+          mq[k] = (int)max((i64)-128, min((i64)127, step_m_round_tie(p2, c.com_mm, seed, stream, row,
                                                                     (uint32_t)(16 * j + 4 * q + k))));
         }
       }
-      wo[q] = pack4(wq[0], wq[1], wq[2], wq[3]);
-      mo[q] = pack4(mq[0], mq[1], mq[2], mq[3]);
+      wo[q] = pack4_cvt(wq[0], wq[1], wq[2], wq[3]);
+      mo[q] = pack4_sat127(mq[0], mq[1], mq[2], mq[3]);
     }
     rsum += (u64)(unsigned)rsum32;
     *reinterpret_cast<int4*>(wr + 16 * j) = make_int4(wo[0], wo[1], wo[2], wo[3]);

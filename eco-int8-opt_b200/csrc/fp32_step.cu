@@ -18,7 +18,8 @@
 // operation here, in the reference's order, with the semantics of PyTorch's CUDA kernels
 // for those operations: a tensor times / plus a Python scalar rounds the scalar to fp32
 // first; `a.add_(b, alpha=c)` is fma(c, b, a); a tensor divided by a Python scalar is a
-// multiply by the fp32 reciprocal; `scalar / tensor` is the tensor's reciprocal times
+// multiply by the scalar's reciprocal taken in double and rounded to fp32 (so
+// v / (1 - 0.999) is v * 1000.0f, not v * 999.99994f); `scalar / tensor` is the tensor's reciprocal times
 // the scalar; addcmul is a + (c * b) * b'.  The norm is sqrt of the double sum of
 // squares, rounded to fp32 (PyTorch's fp32 reduction can differ from it in the last
 // bit, which changes the clip factor only when clipping is active).
@@ -231,7 +232,7 @@ extern "C" int eco_fp32_eco_step(const eco_fp32_layer_t* layers, int n_layers, c
   P.esum = scratch + 2 * tiles;
   const eco_fp32_hyper_t& H = *hyper;
   // PyTorch turns a Python scalar operand into the op's dtype (fp32), and divides by one
-  // through the fp32 reciprocal computed on the host
+  // as a multiply by its reciprocal, computed in double and rounded to fp32
   P.b_f = (float)H.beta1;
   P.omb_f = (float)(1.0 - H.beta1);
   P.lr_f = (float)H.lr;
@@ -242,8 +243,8 @@ extern "C" int eco_fp32_eco_step(const eco_fp32_layer_t* layers, int n_layers, c
   P.omb2_f = (float)(1.0 - H.beta2);
   P.adam_eps_f = (float)H.eps;
   P.bc1_f = (float)H.bc1;
-  P.inv_bc1 = 1.0f / (float)H.bc1;
-  P.inv_bc2 = 1.0f / (float)H.bc2;
+  P.inv_bc1 = (float)(1.0 / H.bc1);
+  P.inv_bc2 = (float)(1.0 / H.bc2);
   P.cinj_f = (float)(1.0 - 1.0 / H.beta1);  // eco.py:223
   cudaStream_t s = eco_stream(stream);
   const unsigned grid = (unsigned)std::max<i64>(1, std::min<i64>(tiles, (i64)eco_num_sms() * 8));

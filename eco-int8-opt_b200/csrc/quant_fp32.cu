@@ -5,8 +5,8 @@
 //   a = max |x|;  s = calc_scale(a) = (a < 1e-8 ? 1 : a / 127)   (Python double arithmetic)
 //   q = clamp(round(x / (s + 1e-8)), -127, 127)                     (quant.py:21-28)
 //
-// PyTorch divides a CUDA tensor by a Python scalar as a multiply by the fp32 reciprocal of
-// the scalar, and torch.round rounds half to even; both are reproduced here, so q is the
+// PyTorch divides a CUDA tensor by a Python scalar as a multiply by the scalar's
+// reciprocal, taken in double and rounded to fp32, and torch.round rounds half to even; both are reproduced here, so q is the
 // reference's bit for bit.  s goes to the device as double bits (scale_out[0]), where the
 // dequantizing GEMM epilogue reads it.
 #include <algorithm>
@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(kThreads) quantize_f32_kernel(const float* __r
                                                                 int64_t* scale_out) {
   const double a = (double)__uint_as_float(*amax);
   const double s = a < 1e-8 ? 1.0 : __ddiv_rn(a, 127.0);  // calc_scale (quant.py:9-16)
-  const float inv = __fdiv_rn(1.0f, __double2float_rn(__dadd_rn(s, 1e-8)));
+  const float inv = __double2float_rn(__ddiv_rn(1.0, __dadd_rn(s, 1e-8)));
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     scale_out[0] = __double_as_longlong(s);
     scale_out[1] = 0;

@@ -7,7 +7,8 @@
 // Each element operation is one IEEE fp32 operation in the reference's order
 // (no fused multiply-add).  The two divisions by 127 of the host glue follow
 // PyTorch's CUDA kernel for a tensor divided by a Python scalar: a multiply
-// by the fp32 reciprocal 1/127.
+// by the reciprocal 1/127 (taken in double and rounded to fp32, which for 127
+// is also the fp32 quotient 1.0f / 127.0f).
 //
 // Work per element: the reference draws five Philox4x32-10 words per element (two in
 // pass 1, three in pass 2, each from its own counter), so the passes are bound by the

@@ -15,8 +15,9 @@ Follows the two-pass algorithm of ``ecoint8/triton_kernels.py`` (v0.4.9):
 Every operation is one IEEE fp32 operation in the order written (no fused
 multiply-add), which is what Triton's interpreter computes.  The two scalar
 divisions by 127 follow either PyTorch's CPU kernel (``division="cpu"``: a true
-division) or its CUDA kernel, which multiplies by the fp32 reciprocal when the
-divisor is a CPU scalar (``division="cuda"``).
+division) or its CUDA kernel, which multiplies by the reciprocal (taken in double,
+rounded to fp32; for 127 that equals the fp32 reciprocal) when the divisor is a CPU
+scalar (``division="cuda"``).
 """
 
 from __future__ import annotations

@@ -57,3 +57,21 @@ def test_int8_linear_trains_with_eco_optimizers():
         acc = (l2(torch.relu(l1(X))).argmax(1) == y).float().mean().item()
         assert acc > 0.85, (type(opt).__name__, acc)
         assert opt.stats["mean_abs_e"] > 0.0
+
+
+def test_dynamic_quantization_over_many_scales():
+    """``quantize_tensor_dynamic`` divides by the Python scalar ``s + EPS``; PyTorch's CUDA
+    kernel multiplies by that scalar's reciprocal taken in double and rounded to fp32, which
+    differs from the fp32 quotient ``1.0f / float(s + EPS)`` for about a quarter of all
+    scales.  Sixty-four tensors with spread-out maxima pin the device quantizer to it."""
+    from ecoint8 import _ops
+    from oracle import float_layers as fl
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(11)
+    for i in range(64):
+        x = torch.randn(37, 129, device=dev, generator=gen) * (10.0 ** (i / 16.0 - 2.0))
+        q, s = _ops.quantize_dynamic(x)
+        want_q, want_s = fl.quantize_tensor_dynamic(x)
+        assert s.value() == want_s
+        assert torch.equal(q, want_q), i
