@@ -42,6 +42,7 @@ constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr unsigned long long kWaitNs = 4000000000ull;  // 4 s bound on any single wait
 constexpr int kGroupM = 16;                            // M tiles per raster group (L2 reuse)
+constexpr int kStageBytes = kEpiWarps * 4096;          // epilogue row staging, 4 KB per warp
 
 template <int BN>
 struct Cfg {
@@ -49,7 +50,7 @@ struct Cfg {
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = S * (A_BYTES + B_BYTES) + 1024 /*barriers*/ + 1024 /*align*/;
+  static constexpr int SMEM = S * (A_BYTES + B_BYTES) + 1024 /*barriers*/ + kStageBytes + 1024 /*align*/;
 };
 
 struct GemmParams {
@@ -173,31 +174,74 @@ ECO_DEV uint32_t idesc_s8(int n, int a_mn, int b_mn) {
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
+// A warp's 32 x 32-word chunk (lane = row) written to rows that are not 16-byte aligned
+// or that end inside the chunk: staged in the warp's 4 KB of shared memory, then stored
+// one row per instruction (lane = column), so a store covers 128 contiguous bytes instead
+// of 32 scattered words.  Row r's 16-byte group g sits at group g ^ (r & 7), which keeps
+// both the 16-byte writes and the row reads free of bank conflicts.
+ECO_DEV void stage_store_rows32(uint32_t* stage, const uint32_t (&w)[32], int lane, uint32_t* row0, i64 ld,
+                                int rows_left, int cols_left) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    *reinterpret_cast<uint4*>(stage + lane * 32 + ((g ^ (lane & 7)) << 2)) =
+        make_uint4(w[4 * g], w[4 * g + 1], w[4 * g + 2], w[4 * g + 3]);
+  __syncwarp();
+  const int rows = min(rows_left, 32);
+#pragma unroll 4
+  for (int r = 0; r < rows; ++r) {
+    const uint32_t x = stage[r * 32 + ((((lane >> 2) ^ (r & 7)) << 2) | (lane & 3))];
+    if (lane < cols_left) row0[r * ld + lane] = x;
+  }
+  __syncwarp();
+}
+
+// The same for a 32 x 32-byte chunk of int8 rows (lane = row holds 8 packed words).
+// Row r's 16-byte halves sit at half h ^ ((r >> 2) & 1).
+ECO_DEV void stage_store_rows8(uint32_t* stage, const uint32_t (&packed)[8], int lane, int8_t* row0, i64 ld,
+                               int rows_left, int cols_left) {
+  uint8_t* sb = reinterpret_cast<uint8_t*>(stage);
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    *reinterpret_cast<uint4*>(sb + lane * 32 + ((h ^ ((lane >> 2) & 1)) << 4)) =
+        make_uint4(packed[4 * h], packed[4 * h + 1], packed[4 * h + 2], packed[4 * h + 3]);
+  __syncwarp();
+  const int rows = min(rows_left, 32);
+#pragma unroll 4
+  for (int r = 0; r < rows; ++r) {
+    const uint8_t x = sb[r * 32 + ((((lane >> 4) ^ ((r >> 2) & 1))) << 4) + (lane & 15)];
+    if (lane < cols_left) row0[r * ld + lane] = (int8_t)x;
+  }
+  __syncwarp();
+}
+
 // int32 epilogue for one 32-column chunk of one row: bias add, max|C|, store.
-ECO_DEV void epi_store_s32(const GemmParams& p, const uint32_t (&v)[32], int m, int nb, int bias_lane, i64& amax) {
-  int o[32];
+ECO_DEV void epi_store_s32(const GemmParams& p, const uint32_t (&v)[32], int m, int nb, int bias_lane, i64& amax,
+                           uint32_t* stage, int lane) {
+  uint32_t o[32];
 #pragma unroll
   for (int e = 0; e < 32; ++e) {
-    o[e] = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
-    const int a = (int)(o[e] < 0 ? 0u - (unsigned)o[e] : (unsigned)o[e]);
+    const int x = add32((int)v[e], __shfl_sync(0xffffffffu, bias_lane, e));
+    o[e] = (uint32_t)x;
+    const int a = (int)(x < 0 ? 0u - (unsigned)x : (unsigned)x);
     if (nb + e < p.N && m < p.M) amax = max(amax, (i64)a);
   }
-  if (m >= p.M) return;
-  int32_t* dst = p.C + (i64)m * p.ldc + nb;
-  if (nb + 32 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
+  if (nb + 32 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {  // warp-uniform
+    if (m >= p.M) return;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(p.C + (i64)m * p.ldc + nb);
 #pragma unroll
-    for (int e = 0; e < 32; e += 4) *reinterpret_cast<int4*>(dst + e) = make_int4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+    for (int e = 0; e < 32; e += 4) *reinterpret_cast<uint4*>(dst + e) = make_uint4(o[e], o[e + 1], o[e + 2], o[e + 3]);
   } else {
-#pragma unroll
-    for (int e = 0; e < 32; ++e)
-      if (nb + e < p.N) dst[e] = o[e];
+    const int m0 = m - lane;
+    stage_store_rows32(stage, o, lane, reinterpret_cast<uint32_t*>(p.C + (i64)m0 * p.ldc + nb), p.ldc, p.M - m0,
+                       p.N - nb);
   }
 }
 
 // Fused requant epilogue for one 32-column chunk of one row: one Philox call per
 // four columns (the element's 32-bit field; exact tie-break draws only when needed).
 ECO_DEV void epi_store_requant(const GemmParams& p, const eco_sr_t& sr, const PhiloxKeys& keys,
-                               const uint32_t (&v)[32], int m, int nb, int bias_lane, int mult_lane) {
+                               const uint32_t (&v)[32], int m, int nb, int bias_lane, int mult_lane, uint32_t* stage,
+                               int lane) {
   uint32_t packed[8];
   const uint32_t row = (uint32_t)(sr.row_base + m);
   const bool philox = sr.mode == ECO_SR_PHILOX && p.shift >= 0;
@@ -269,15 +313,14 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const eco_sr_t& sr, const Ph
     }
   }
   }
-  if (m >= p.M) return;
-  int8_t* dst = p.Y + (i64)m * p.ldy + nb;
-  if (nb + 32 <= p.N && (p.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15) == 0) {
+  if (nb + 32 <= p.N && (p.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(p.Y) & 15) == 0) {  // warp-uniform
+    if (m >= p.M) return;
+    int8_t* dst = p.Y + (i64)m * p.ldy + nb;
     *reinterpret_cast<int4*>(dst) = make_int4(packed[0], packed[1], packed[2], packed[3]);
     *reinterpret_cast<int4*>(dst + 16) = make_int4(packed[4], packed[5], packed[6], packed[7]);
   } else {
-#pragma unroll
-    for (int e = 0; e < 32; ++e)
-      if (nb + e < p.N) dst[e] = (int8_t)(packed[e / 4] >> (8 * (e % 4)));
+    const int m0 = m - lane;
+    stage_store_rows8(stage, packed, lane, p.Y + (i64)m0 * p.ldy + nb, p.ldy, p.M - m0, p.N - nb);
   }
 }
 
@@ -286,24 +329,24 @@ ECO_DEV void epi_store_requant(const GemmParams& p, const eco_sr_t& sr, const Ph
 // fp32 operation like PyTorch's kernels; the scalar is the fp32 rounding of the double
 // product sa * sb (a Python float, or a product of two, in the reference).
 ECO_DEV void epi_store_dequant(const GemmParams& p, float scalar, const uint32_t (&v)[32], int m, int nb,
-                               float cs_lane, float bias_lane) {
-  float o[32];
+                               float cs_lane, float bias_lane, uint32_t* stage, int lane) {
+  uint32_t o[32];
 #pragma unroll
   for (int e = 0; e < 32; ++e) {  // every lane shuffles (row m may be past the end)
     float y = __fmul_rn(__int2float_rn((int)v[e]), scalar);
     if (p.col_scale) y = __fmul_rn(y, __shfl_sync(0xffffffffu, cs_lane, e));
     if (p.bias_f) y = __fadd_rn(y, __shfl_sync(0xffffffffu, bias_lane, e));
-    o[e] = y;
+    o[e] = __float_as_uint(y);
   }
-  if (m >= p.M) return;
-  float* dst = p.Yf + (i64)m * p.ldyf + nb;
-  if (nb + 32 <= p.N && (p.ldyf & 3) == 0 && (reinterpret_cast<uintptr_t>(p.Yf) & 15) == 0) {
+  if (nb + 32 <= p.N && (p.ldyf & 3) == 0 && (reinterpret_cast<uintptr_t>(p.Yf) & 15) == 0) {  // warp-uniform
+    if (m >= p.M) return;
+    uint32_t* dst = reinterpret_cast<uint32_t*>(p.Yf + (i64)m * p.ldyf + nb);
 #pragma unroll
-    for (int e = 0; e < 32; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+    for (int e = 0; e < 32; e += 4) *reinterpret_cast<uint4*>(dst + e) = make_uint4(o[e], o[e + 1], o[e + 2], o[e + 3]);
   } else {
-#pragma unroll
-    for (int e = 0; e < 32; ++e)
-      if (nb + e < p.N) dst[e] = o[e];
+    const int m0 = m - lane;
+    stage_store_rows32(stage, o, lane, reinterpret_cast<uint32_t*>(p.Yf + (i64)m0 * p.ldyf + nb), p.ldyf, p.M - m0,
+                       p.N - nb);
   }
 }
 
@@ -427,6 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int e = warp - 2;
     const int q = warp & 3;           // TMEM lane quarter this warp may access
     const int half = e >> 2;          // which half of the BN columns
+    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + S * (C::A_BYTES + C::B_BYTES) + 1024) + e * 1024;
     constexpr int kChunks = BN / 64;  // 32-column chunks per half
     i64 amax = 0;
     int j = 0;
@@ -459,15 +503,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (EPI == 2) {
           const float cs = (p.col_scale && n_lane < p.N) ? __ldg(p.col_scale + n_lane) : 0.0f;
           const float bf = (p.bias_f && n_lane < p.N) ? __ldg(p.bias_f + n_lane) : 0.0f;
-          epi_store_dequant(p, scalar, v, m, nb, cs, bf);
+          epi_store_dequant(p, scalar, v, m, nb, cs, bf, stage, lane);
           continue;
         }
         const int bias_lane = (p.bias && n_lane < p.N) ? __ldg(p.bias + n_lane) : 0;
         if (EPI == 0) {
-          epi_store_s32(p, v, m, nb, bias_lane, amax);
+          epi_store_s32(p, v, m, nb, bias_lane, amax, stage, lane);
         } else {
           const int mult_lane = n_lane < p.N ? __ldg(p.mult + n_lane) : 0;
-          epi_store_requant(p, sr, keys, v, m, nb, bias_lane, mult_lane);
+          epi_store_requant(p, sr, keys, v, m, nb, bias_lane, mult_lane, stage, lane);
         }
       }
       tc_fence_before();
@@ -504,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int PBN = 256;                         // tile N (both CTAs)
 constexpr int PHALF_B = (PBN / 2) * BK;          // B bytes per CTA and stage
 constexpr int PS = 6;                            // stages
-constexpr int PSMEM = PS * (BM * BK + PHALF_B) + 1024 + 1024;
+constexpr int PSMEM = PS * (BM * BK + PHALF_B) + 1024 + kStageBytes + 1024;
 
 ECO_DEV uint32_t cluster_rank() {
   uint32_t r;
@@ -674,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int half = e >> 2;
     constexpr int kChunks = PBN / 64;
+    uint32_t* stage = reinterpret_cast<uint32_t*>(smem + S * (A_BYTES + B_BYTES) + 1024) + e * 1024;
     PhiloxKeys keys;
     const eco_sr_t sr = sr_resolve(p.sr, p.keys, keys);
     float scalar = 0.0f;
@@ -706,15 +751,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (EPI == 2) {
           const float cs = (p.col_scale && n_lane < p.N) ? __ldg(p.col_scale + n_lane) : 0.0f;
           const float bf = (p.bias_f && n_lane < p.N) ? __ldg(p.bias_f + n_lane) : 0.0f;
-          epi_store_dequant(p, scalar, v, m, nb, cs, bf);
+          epi_store_dequant(p, scalar, v, m, nb, cs, bf, stage, lane);
           continue;
         }
         const int bias_lane = (p.bias && n_lane < p.N) ? __ldg(p.bias + n_lane) : 0;
         if (EPI == 0) {
-          epi_store_s32(p, v, m, nb, bias_lane, amax);
+          epi_store_s32(p, v, m, nb, bias_lane, amax, stage, lane);
         } else {
           const int mult_lane = n_lane < p.N ? __ldg(p.mult + n_lane) : 0;
-          epi_store_requant(p, sr, keys, v, m, nb, bias_lane, mult_lane);
+          epi_store_requant(p, sr, keys, v, m, nb, bias_lane, mult_lane, stage, lane);
         }
       }
       tc_fence_before();
