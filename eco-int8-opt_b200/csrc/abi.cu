@@ -1,6 +1,7 @@
 // C-ABI housekeeping: version, last error, device support, shared checks.
 #include "abi.cuh"
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -52,11 +53,46 @@ extern "C" int eco_device_supported(int device) {
   return (major == 10 && minor == 0) ? 1 : 0;
 }
 
+namespace {
+// Row copy into a destination whose rows start on 16-byte boundaries, from rows of any
+// alignment (the relayout of an operand for the GEMM's TMA loads): a thread writes one
+// 16-byte chunk, assembled by funnel shifts from the aligned 4-byte words that hold its
+// 16 source bytes (every word read holds at least one byte of the row, so no read leaves
+// the row's words); a row's last chunk, when shorter than 16 bytes, is copied bytewise.
+__global__ void copy_rows_to_aligned_kernel(const int8_t* __restrict__ src, int64_t ld_src, int8_t* __restrict__ dst,
+                                            int64_t ld_dst, int64_t rows, int64_t cols) {
+  const int64_t nchunk = (cols + 15) / 16;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nchunk) return;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const int8_t* s = src + r * ld_src + 16 * i;
+    int8_t* d = dst + r * ld_dst + 16 * i;
+    if (16 * i + 16 <= cols) {
+      const uintptr_t a = reinterpret_cast<uintptr_t>(s);
+      const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+      const uint32_t sh = (uint32_t)(a & 3) * 8;
+      const uint32_t w0 = __ldg(w), w1 = __ldg(w + 1), w2 = __ldg(w + 2), w3 = __ldg(w + 3);
+      const uint32_t w4 = sh ? __ldg(w + 4) : 0u;
+      *reinterpret_cast<uint4*>(d) = make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh),
+                                                __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh));
+    } else {
+      for (int64_t b = 0; b < cols - 16 * i; ++b) d[b] = s[b];
+    }
+  }
+}
+}  // namespace
+
 extern "C" int eco_copy2d_s8(const int8_t* src, int64_t ld_src, int8_t* dst, int64_t ld_dst,
                              int64_t rows, int64_t cols, eco_stream_t stream) {
   ECO_REQUIRE(src && dst && rows >= 0 && cols >= 0 && ld_src >= cols && ld_dst >= cols, ECO_ERR_ARG,
               "eco_copy2d_s8: bad arguments");
   if (rows == 0 || cols == 0) return ECO_OK;
+  if (eco_aligned16(dst) && ld_dst % 16 == 0) {
+    const int64_t nchunk = (cols + 15) / 16;
+    const dim3 grid((unsigned)((nchunk + 127) / 128), (unsigned)std::min<int64_t>(rows, 32768));
+    copy_rows_to_aligned_kernel<<<grid, 128, 0, eco_stream(stream)>>>(src, ld_src, dst, ld_dst, rows, cols);
+    return eco_launch_check("eco_copy2d_s8");
+  }
   cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)ld_dst, src, (size_t)ld_src, (size_t)cols, (size_t)rows,
                                     cudaMemcpyDeviceToDevice, eco_stream(stream));
   if (e != cudaSuccess) return eco_fail(ECO_ERR_LAUNCH, "eco_copy2d_s8: %s", cudaGetErrorString(e));

@@ -172,6 +172,25 @@ def test_split_cols_matches_block_transpose():
         assert torch.equal(dst, want), (rows, cols, parts)
 
 
+def test_copy2d_relayout_from_any_alignment():
+    """eco_copy2d_s8 (the operand relayout before the GEMM's 16-byte TMA rows): rows of any
+    start offset and width into a 16-byte aligned buffer, and into an unaligned one (the
+    library's generic 2-D copy); bytes outside the copied columns are left alone."""
+    from ecoint8 import _native
+
+    gen = torch.Generator().manual_seed(4)
+    for rows, cols, ld, off in [(1, 1, 1, 0), (3, 17, 19, 1), (5, 16, 16, 3), (64, 4097, 4097, 0), (9, 35, 40, 2),
+                                (300, 1000, 1003, 1), (2, 20, 21, 3)]:
+        flat = torch.randint(-127, 128, (off + rows * ld + 5,), dtype=torch.int8, generator=gen).cuda()
+        src = flat[off:off + rows * ld].view(rows, ld)[:, :cols]
+        for ld_dst, dst_off in [((cols + 15) // 16 * 16, 0), (cols + 3, 1)]:
+            base = torch.full((dst_off + rows * ld_dst,), 55, dtype=torch.int8, device="cuda")
+            dst = base[dst_off:].view(rows, ld_dst)
+            _native.call("eco_copy2d_s8", src.data_ptr(), ld, dst.data_ptr(), ld_dst, rows, cols, _native.stream())
+            assert torch.equal(dst[:, :cols], src), (rows, cols, ld, off, ld_dst)
+            assert bool((dst[:, cols:] == 55).all()) and bool((base[:dst_off] == 55).all())
+
+
 def test_peer_push_signal_and_bounded_wait_on_one_gpu():
     """The peer-exchange kernels with this GPU's own buffers as the only 'peer': both
     push modes land where the layout says, a signalled slot releases the wait, and
