@@ -77,6 +77,16 @@ ECO_DEV int sbyte(uint32_t x, int k) {
 ECO_DEV uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
+// Four int32 saturated to [-128, 127] and packed into bytes (a lowest): two saturating
+// pack conversions.
+ECO_DEV uint32_t pack4_sat(int a, int b, int c, int d) {
+  uint32_t hi, r;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(d), "r"(c));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
+  return r;
+}
+// The same saturated to [-127, 127]: one per-byte max with -127 after the packs.
+ECO_DEV uint32_t pack4_sat127(int a, int b, int c, int d) { return __vmaxs4(pack4_sat(a, b, c, d), 0x81818181u); }
 
 // ---------------------------------------------------------------- Philox4x32-10
 // Salmon et al., "Parallel random numbers: as easy as 1, 2, 3" (SC'11).

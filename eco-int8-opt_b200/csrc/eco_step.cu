@@ -181,23 +181,6 @@ ECO_DEV void eco_elem_fast(const FastRow& c, int w, int m, int g, int nw, int& m
   m_new_out = m_new;
 }
 
-// Four int32 saturated to [-127, 127] and packed into bytes (a lowest): two saturating
-// pack conversions (to [-128, 127]) and one per-byte max with -127.
-ECO_DEV uint32_t pack4_sat127(int a, int b, int c, int d) {
-  uint32_t hi, r;
-  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(d), "r"(c));
-  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
-  return __vmaxs4(r, 0x81818181u);
-}
-
-// Four int32 in [-128, 127] packed into bytes (a lowest): two pack conversions.
-ECO_DEV uint32_t pack4_cvt(int a, int b, int c, int d) {
-  uint32_t hi, r;
-  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(d), "r"(c));
-  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(b), "r"(a), "r"(hi));
-  return r;
-}
-
 // (x >> s) as int32 (the result fits): the high word shifted when s >= 32 (HI),
 // else one funnel shift.
 template <bool HI>
@@ -277,7 +260,7 @@ ECO_DEV int fast32_row(const RowCtx& c, const PhiloxKeys& keys, u64 seed, u64 st
                                                                     (uint32_t)(16 * j + 4 * q + k))));
         }
       }
-      wo[q] = pack4_cvt(wq[0], wq[1], wq[2], wq[3]);
+      wo[q] = pack4_sat(wq[0], wq[1], wq[2], wq[3]);
       mo[q] = pack4_sat127(mq[0], mq[1], mq[2], mq[3]);
     }
     rsum += (u64)(unsigned)rsum32;

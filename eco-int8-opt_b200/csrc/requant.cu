@@ -167,7 +167,6 @@ ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
   const bool zero_out = sh > 62;
   const int lo = sh - 32;  // BIG: bits of the tie-break draw
   const uint32_t pow2lo = BIG ? 1u << lo : 0u;
-  const int lower = a.relu ? 0 : -127;
   const int32_t mult_s = (int32_t)(a.dparams ? a.dparams[1] : a.mult_scalar);
   long long sq = 0;
   // The block's work is the chunk sequence (row r, chunk j) with rows blockIdx.x +
@@ -205,7 +204,6 @@ ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
       if (MASK) nm = *reinterpret_cast<const int4*>(a.mask + r * a.ld_mask + j * 16);
     }
     const uint32_t grow = (uint32_t)(sr.row_base + cr);
-    const int8_t* mb = reinterpret_cast<const int8_t*>(&mk);
     const uint32_t* mw = reinterpret_cast<const uint32_t*>(&mk);
     uint32_t packed[4];
     int sq32 = 0;
@@ -213,7 +211,7 @@ ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
     for (int q = 0; q < 4; ++q) {
       const Philox4 rnd = sr_quad_k(keys, sr.stream, grow, (uint32_t)((c0 >> 2) + q));
       int y4[4];
-      unsigned ties = 0u;
+      uint32_t tf[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int e = 4 * q + k;
@@ -226,7 +224,7 @@ ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
         if (BIG) {
           const i64 p2 = mad_wide_u32(f, pow2lo, prod);  // prod + (f << lo)
           // the tie-break draw matters only when bits [lo, lo + 32) of p2 are all ones
-          ties |= (unsigned)(__funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo) == 0xFFFFFFFFu) << k;
+          tf[k] = __funnelshift_r(lo32(p2), (uint32_t)hi32(p2), lo);
           y = hi32(p2) >> lo;  // (p2 >> shift) fits int32
         } else if (sh >= 0 && !zero_out) {
           const u64 u = sh == 32 ? (u64)f : (u64)(f & ((1u << sh) - 1u));
@@ -240,10 +238,11 @@ ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
         }
         y4[k] = y;
       }
-      if (BIG && ties) {  // rare (2^-32 per element): redo the tied elements with the exact draw
+      // rare (2^-32 per element): the tied elements take the exact draw
+      if (BIG && __vimax3_u32(__vimax3_u32(tf[0], tf[1], tf[2]), tf[3], 0u) == 0xFFFFFFFFu) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          if (!((ties >> k) & 1u)) continue;
+          if (tf[k] != 0xFFFFFFFFu) continue;
           const int c = c0 + 4 * q + k;
           int x = v[4 * q + k];
           if (BIAS) x = add32(x, a.bias[c]);
@@ -252,15 +251,10 @@ ECO_DEV void requant_philox_body(const RequantArgs& a, int sh) {
                                                              grow, (uint32_t)c)));
         }
       }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        int y = max(min(y4[k], 127), lower);  // saturate, ReLU
-        if (MASK && SUMSQ && mb[4 * q + k] <= 0) y = 0;
-        if (SUMSQ) sq32 += y * y;
-        y4[k] = y;
-      }
-      packed[q] = pack4(y4[0], y4[1], y4[2], y4[3]);
-      if (MASK && !SUMSQ) packed[q] &= bytes_positive(mw[q]);
+      // saturate to [-128, 127] in the packs, then to [-127 or 0 (ReLU), 127] per byte
+      packed[q] = __vmaxs4(pack4_sat(y4[0], y4[1], y4[2], y4[3]), a.relu ? 0u : 0x81818181u);
+      if (MASK) packed[q] &= bytes_positive(mw[q]);
+      if (SUMSQ) sq32 = __dp4a((int)packed[q], (int)packed[q], sq32);  // the four squares
     }
     if (SUMSQ) sq += sq32;
     *reinterpret_cast<int4*>(a.dst + cr * a.ld_dst + c0) = make_int4(packed[0], packed[1], packed[2], packed[3]);
