@@ -18,10 +18,18 @@ pytestmark = pytest.mark.gpu
 
 
 def test_torch_cuda_divides_by_scalar_via_reciprocal():
+    """PyTorch's CUDA kernel divides an fp32 tensor by a Python scalar as a multiply by the
+    scalar's reciprocal taken in double and rounded to fp32.  For 127 that is also the fp32
+    quotient 1.0f / 127.0f; for 1 - 0.999 (Adam's second bias correction at step 1) the two
+    differ (1000.0f against 999.99994f), and the double one is PyTorch's."""
     x = torch.rand(1 << 16, generator=torch.Generator().manual_seed(1)) * 3.0
     got = (x.cuda() / 127.0).cpu().numpy()
     ref = (x.numpy() * np.float32(np.float32(1.0) / np.float32(127.0))).astype(np.float32)
     assert np.array_equal(got, ref)
+    d = 1.0 - 0.999
+    got = (x.cuda() / d).cpu().numpy()
+    assert np.array_equal(got, (x.numpy() * np.float32(1.0 / d)).astype(np.float32))
+    assert not np.array_equal(got, (x.numpy() * (np.float32(1.0) / np.float32(d))).astype(np.float32))
 
 
 @pytest.mark.parametrize("rows,cols,wd,seed", [(8, 300, 0.0, 1234), (5, 1000, 0.01, 77), (33, 64, 0.0, 5),
