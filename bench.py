@@ -134,7 +134,8 @@ KERNELS_PER_CALL = {"eco_gemm_s8s32": 1, "eco_gemm_s8_requant": 1, "eco_requant_
                     "eco_i8eco_step": _step_kernels, "eco_i8eco_finalize": 1, "eco_sgdm_step": 3,
                     "eco_peer_push_s8": 1, "eco_peer_push_signal_s8": 1, "eco_peer_signal": 1,
                     "eco_peer_wait": 1, "eco_peer_allreduce_i64": 1, "eco_ce_grad_rowstats": 1,
-                    "eco_ce_grad_quantize": 1}
+                    "eco_ce_grad_quantize": 1, "eco_copy2d_s8": 1, "eco_gemm_s8_dequant": 1,
+                    "eco_quantize_dynamic_f32": 2, "eco_fp32_eco_step": 2}
 
 
 class LaunchCounter:

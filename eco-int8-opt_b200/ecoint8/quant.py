@@ -119,12 +119,14 @@ def cross_entropy_grad_i8(logits_i8: torch.Tensor, s_out, labels: torch.Tensor, 
         spec = nat.sr_spec(nat.SR_PHILOX, seed=_sr.new_key(), stream_id=0, row_base=_sr.row_base())
         if _sr.LOG is not None:
             _sr.LOG.append(("boundary", spec.seed, 0, (rows, cols), 24, spec.row_base))
-    g = torch.empty((rows, cols), dtype=torch.int8, device=dev)
+    # rows padded to 16 bytes: the backward's GEMMs read g in place (TMA rows), no relayout
+    ld_g = (cols + 15) // 16 * 16
+    g = torch.empty((rows, ld_g), dtype=torch.int8, device=dev)[:, :cols]
     g_fp = torch.empty((rows, cols), dtype=torch.float32, device=dev) if return_fp32 else None
     scale = torch.empty(3, dtype=torch.int64, device=dev)
     loss = torch.empty((), dtype=torch.float32, device=dev)
     nat.call("eco_ce_grad_quantize", x.data_ptr(), rows, cols, ld, s_out, labels.data_ptr(), count,
-             stats.data_ptr(), amax_src.data_ptr(), bits, spec, g.data_ptr(), cols, nat.ptr(g_fp), scale.data_ptr(),
+             stats.data_ptr(), amax_src.data_ptr(), bits, spec, g.data_ptr(), ld_g, nat.ptr(g_fp), scale.data_ptr(),
              row_loss.data_ptr(), loss.data_ptr(), nat.stream())
     s_g = _scale.DevScale(scale)
     return (loss, g, s_g, g_fp) if return_fp32 else (loss, g, s_g)
