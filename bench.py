@@ -144,12 +144,18 @@ class LaunchCounter:
 
         self.nat = _native
         self.count = 0
+        self.captured = 0  # of which recorded into a CUDA graph
         self.orig = _native.call
 
     def __enter__(self):
+        from ecoint8 import graphs
+
         def counting(name, *args):
             k = KERNELS_PER_CALL.get(name, 0)
-            self.count += k(*args) if callable(k) else k
+            k = k(*args) if callable(k) else k
+            self.count += k
+            if graphs.capturing() is not None:
+                self.captured += k
             return self.orig(name, *args)
 
         self.nat.call = counting
@@ -585,6 +591,7 @@ def main():
     ap.add_argument("--only", choices=["gemm", "gemm_sweep", "eco_step", "requant", "sgdm", "peak"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
+    ap.add_argument("--sgdm-layers", type=int, default=64, help="layers of 4096x4096 in the EcoInt8SGDM measurement")
     ap.add_argument("--dw-exchange", default="peer", choices=["gather", "reduce", "peer"],
                     help="how ranks form the summed dW rows (ecoint8.parallel.init)")
     ap.add_argument("--comm-sms", type=int, default=16, help="SMs the GEMMs leave to the exchange under data parallelism")
@@ -609,7 +616,7 @@ def main():
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
         res = {"gemm": lambda: gemm_measurements(dev)[0], "gemm_sweep": lambda: gemm_sweep(dev),
-               "requant": lambda: requant_measurement(dev), "sgdm": lambda: sgdm_measurement(dev),
+               "requant": lambda: requant_measurement(dev), "sgdm": lambda: sgdm_measurement(dev, layers=args.sgdm_layers),
                "peak": lambda: int8_peak(dev),
                "eco_step": lambda: eco_step_measurement(dev, layers=args.eco_layers)}[args.only]()
         print(json.dumps({args.only: res}))
@@ -655,12 +662,12 @@ def main():
             from ecoint8.graphs import StepGraph
 
             # the first warm-up step runs eagerly inside capture(); the graph then holds
-            # exactly one step's launches, counted while it is recorded
+            # one step's launches, counted while they are recorded
             graph = StepGraph(lambda: train_step(net, opt, x_i8, y), warmup=1)
             counter = LaunchCounter()
             with counter:
                 graph.capture()
-            graph_launches = counter.count // 2  # the eager warm-up step + the recorded step
+            graph_launches = counter.captured  # the launches recorded in the graph
             for _ in range(args.warmup - 1):
                 graph.replay()
         step = graph.replay if graph is not None else (lambda: train_step(net, opt, x_i8, y))
@@ -682,7 +689,9 @@ def main():
             torch.cuda.synchronize()
             barrier()
         ms = ev0.elapsed_time(ev1)
-        launches = graph_launches if graph is not None else counter.count // args.steps
+        # with a graph: its recorded launches plus those issued after each replay (the weight
+        # rows' pushes of the data-parallel exchange)
+        launches = (graph_launches if graph is not None else 0) + counter.count // args.steps
         # e2e: the same steps through the public API with the int8 batch and labels coming
         # from pinned host memory and the loss read back every step; like a data loader,
         # the next step's batch crosses PCIe on a copy stream while this step computes

@@ -395,6 +395,17 @@ def gather_rows(layer, rows) -> None:
     stepped in full on every rank)."""
     bufs = peer_bufs(layer)
     if bufs is not None:
+        from . import graphs
+
+        g = graphs.capturing()
+        if g is not None:
+            # Not recorded: a captured step joins its side streams before it ends, so a push
+            # inside the graph would hold every replay until it finished.  Each replay is
+            # followed by the push instead, queued behind it on the communication stream, and
+            # the next replay's forward waits for it on the device -- the overlap an
+            # uncaptured step gets.
+            g.on_replay(lambda b=bufs, lo=rows[0], hi=rows[1]: _PEER.push_weight_rows(b, lo, hi))
+            return
         _PEER.push_weight_rows(bufs, rows[0], rows[1])
         return
     layer._gather_works = [dist.all_gather_into_tensor(layer.w_i8, layer.w_i8[rows[0]:rows[1]], group=_GROUP,

@@ -150,9 +150,13 @@ def test_reductions_colsum_amax_sumsq():
     from ecoint8 import _ops
 
     gen = torch.Generator().manual_seed(2)
-    for rows, cols in [(1, 1), (5, 3), (16384, 10), (300, 8192)]:
+    for rows, cols in [(1, 1), (5, 3), (16384, 10), (300, 8192), (16384, 1000), (7, 48), (1, 40), (2000, 4104)]:
         g = torch.randint(-127, 128, (rows, cols), dtype=torch.int8, generator=gen)
         assert torch.equal(_ops.colsum(g.cuda()).cpu(), g.to(torch.int64).sum(0))
+        # a view with 16-byte padded rows (the loss boundary's layout): 16 columns per thread
+        pad = torch.zeros((rows, (cols + 15) // 16 * 16), dtype=torch.int8)
+        pad[:, :cols] = g
+        assert torch.equal(_ops.colsum(pad.cuda()[:, :cols]).cpu(), g.to(torch.int64).sum(0))
         assert int(_ops.sumsq(g.cuda()).item()) == int((g.to(torch.int64) ** 2).sum())
         x = torch.randint(-(1 << 31) + 1, 1 << 31, (rows, cols), dtype=torch.int64, generator=gen).to(torch.int32)
         assert int(_ops.amax(x.cuda()).item()) == int(x.to(torch.int64).abs().max())
