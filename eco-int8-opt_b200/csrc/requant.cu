@@ -331,8 +331,8 @@ __global__ void __launch_bounds__(kThreads) colsum16_kernel(const int8_t* __rest
 #pragma unroll
   for (int e = 0; e < 16; ++e) sum[e] = 0;
   if (c0 + 16 <= cols) {
-#pragma unroll 4
-    for (i64 r = r0; r < r1; ++r) {
+#pragma unroll 8
+    for (i64 r = r0; r < r1; ++r) {  // eight rows' loads in flight per thread
       const int4 v = __ldg(reinterpret_cast<const int4*>(g + r * ld + c0));
       const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
 #pragma unroll
