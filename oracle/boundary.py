@@ -100,7 +100,7 @@ def mnist_batch(index: int, batch: int = MNIST_B):
     return X, y
 
 
-MNIST_GOLDEN_STEPS = 100  # steps of the MNIST-shaped run pinned by the golden fixture
+MNIST_GOLDEN_STEPS = 469  # steps of the MNIST-shaped run pinned by the golden fixture: one epoch of 60000 at 128
 
 WIDE_D, WIDE_C, WIDE_B = 8192, 1000, 64  # config-5 layer widths, the golden fixture's batch
 

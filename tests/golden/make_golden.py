@@ -194,11 +194,11 @@ def gen_mnist(ref, bnd, nsteps):
     with torch.no_grad():
         x0, sx0 = bnd.quantize_tensor_dynamic(X0, stochastic=False)
         net.calibrate(x0, sx0)
-    opt = I8ECO(net.int8_layers(), lr=bnd.mnist_lr(0, 100), momentum=0.9)
+    opt = I8ECO(net.int8_layers(), lr=bnd.mnist_lr(0, bnd.MNIST_GOLDEN_STEPS), momentum=0.9)
     steps = []
     for t in range(nsteps):
         X, y = bnd.mnist_batch(t)
-        opt.set_lr(bnd.mnist_lr(t, 100))
+        opt.set_lr(bnd.mnist_lr(t, bnd.MNIST_GOLDEN_STEPS))
         with torch.no_grad():
             x_i8, _ = net.quantize_input(X)
             logits, s_out = net.forward_i8(x_i8)

@@ -86,7 +86,7 @@ def test_blob_training_replay_matches_reference_every_step(golden):
 
 
 def test_mnist_shaped_replay_matches_reference(golden):
-    """784-256-128-10 at batch 128 (the MNIST-shaped config), first steps bit-exact."""
+    """784-256-128-10 at batch 128 (the MNIST-shaped config): one epoch (469 steps), every step bit-exact."""
     import ecoint8
     from ecoint8 import I8ECO, I8Linear, I8ReLU, I8Sequential
 
@@ -98,10 +98,10 @@ def test_mnist_shaped_replay_matches_reference(golden):
         X0, _ = bnd.mnist_batch(0)
         x0, sx0 = bnd.quantize_tensor_dynamic(X0, stochastic=False)
         net.calibrate(x0.cuda(), sx0)
-        opt = I8ECO(net.int8_layers(), lr=bnd.mnist_lr(0, 100), momentum=0.9)
+        opt = I8ECO(net.int8_layers(), lr=bnd.mnist_lr(0, bnd.MNIST_GOLDEN_STEPS), momentum=0.9)
         for t, st in enumerate(d["steps"]):
             X, y = bnd.mnist_batch(t)
-            opt.set_lr(bnd.mnist_lr(t, 100))
+            opt.set_lr(bnd.mnist_lr(t, bnd.MNIST_GOLDEN_STEPS))
             x_i8 = net.quantize_input(X)[0].cuda()
             logits, s_out = net.forward_i8(x_i8)
             assert digest(logits) == st["logits"], t

@@ -161,11 +161,11 @@ def test_mnist_shaped_training_bit_exact(golden):
     X0, _ = bnd.mnist_batch(0)
     x0, sx0 = bnd.quantize_tensor_dynamic(X0, stochastic=False)
     net.calibrate(x0.numpy(), sx0, draws)
-    opt = ost.I8ECO(net.int8_layers(), lr=bnd.mnist_lr(0, 100), momentum=0.9)
+    opt = ost.I8ECO(net.int8_layers(), lr=bnd.mnist_lr(0, bnd.MNIST_GOLDEN_STEPS), momentum=0.9)
     sx = net.int8_layers()[0].sx
     for t, st in enumerate(d["steps"]):
         X, y = bnd.mnist_batch(t)
-        opt.set_lr(bnd.mnist_lr(t, 100))
+        opt.set_lr(bnd.mnist_lr(t, bnd.MNIST_GOLDEN_STEPS))
         x_i8 = torch.clamp(torch.round(X / sx), -127, 127).to(torch.int8).numpy()
         logits, s_out = net.forward_i8(x_i8, draws)
         assert digest(logits) == st["logits"], t
