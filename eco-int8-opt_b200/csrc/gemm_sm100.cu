@@ -817,6 +817,17 @@ int make_tmap(CUtensorMap* map, const int8_t* base, i64 inner, i64 outer, i64 ld
 // caller lowers it so that NCCL's kernels find free SMs and overlap the GEMMs.
 int g_gemm_sm_limit = 0;
 
+// Whether a launch's epilogue can take the staged store path (an output whose rows are not
+// 16-byte aligned, or a width that leaves a partial 32-column chunk).  Launches that never
+// stage leave its 32 KB of shared memory out, so that the small kernels of other streams
+// (requants, column sums) still fit on the SMs beside the persistent GEMM.
+bool staging_needed(const GemmParams& p, int epi) {
+  if (p.N % 32 != 0) return true;
+  if (epi == 0) return (p.ldc & 3) != 0 || (reinterpret_cast<uintptr_t>(p.C) & 15) != 0;
+  if (epi == 1) return (p.ldy & 15) != 0 || (reinterpret_cast<uintptr_t>(p.Y) & 15) != 0;
+  return (p.ldyf & 3) != 0 || (reinterpret_cast<uintptr_t>(p.Yf) & 15) != 0;
+}
+
 template <int BN, int EPI>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
   auto kern = gemm_s8_kernel<BN, EPI>;
@@ -833,7 +844,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cu
   int ctas = eco_num_sms();  // persistent: at most one CTA per SM
   if (g_gemm_sm_limit > 0) ctas = std::min(ctas, g_gemm_sm_limit);
   const int grid = std::min(tiles, ctas);
-  kern<<<grid, kThreads, Cfg<BN>::SMEM, s>>>(ta, tb, q);
+  kern<<<grid, kThreads, Cfg<BN>::SMEM - (staging_needed(p, EPI) ? 0 : kStageBytes), s>>>(ta, tb, q);
   return eco_launch_check("gemm_s8_kernel");
 }
 
@@ -867,7 +878,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = PSMEM;
+  cfg.dynamicSmemBytes = PSMEM - (staging_needed(p, EPI) ? 0 : kStageBytes);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

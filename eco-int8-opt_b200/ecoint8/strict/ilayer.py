@@ -156,7 +156,7 @@ class I8Linear(nn.Module):
 
     # Per-call bookkeeping attributes bypass nn.Module.__setattr__ (none is a
     # parameter, buffer or submodule; properties still apply).
-    _PLAIN_ATTRS = frozenset({"_cache_x", "_dw_pending", "_fwd_cache", "_gb_s", "_gb_sum", "_gw_rows", "_gw_s",
+    _PLAIN_ATTRS = frozenset({"_cache_x", "_dw_pending", "_dw_event", "_fwd_cache", "_gb_s", "_gb_sum", "_gw_rows", "_gw_s",
                               "_gw_i8", "_gw_sumsq", "_gw_sumsq_of", "_sw_cache", "_input_gather",
                               "_gather_works"})
 
@@ -170,9 +170,10 @@ class I8Linear(nn.Module):
         """Module state for ``torch.save(model)`` (the reference's way to persist): the
         launch caches and in-flight exchange handles are dropped (rebuilt on use); device
         scales of a queued backward are stored as their float values."""
+        self._grad_get("_gw_i8")  # a queued backward's dW branch has finished before the copy
         d = nn.Module.__getstate__(self) if hasattr(nn.Module, "__getstate__") else dict(self.__dict__)
         d = dict(d)
-        for k in ("_fwd_cache", "_sw_cache", "_input_gather", "_gather_works", "_sw_mean_cache"):
+        for k in ("_fwd_cache", "_sw_cache", "_input_gather", "_gather_works", "_sw_mean_cache", "_dw_event"):
             d.pop(k, None)
         if d.get("_dw_pending") is not None:
             raise RuntimeError("a data-parallel dW reduction is in flight: read a gradient or call "
@@ -190,6 +191,10 @@ class I8Linear(nn.Module):
     def _grad_get(self, name):
         if self.__dict__.get("_dw_pending") is not None:
             parallel.finalize_pending()
+        ev = self.__dict__.get("_dw_event")
+        if ev is not None:  # a queued backward's dW branch: order the reader's stream after it
+            self.__dict__["_dw_event"] = None
+            torch.cuda.current_stream(self.w_i8.device).wait_event(ev)
         return self.__dict__.get(name + "_store")
 
     _gw_i8 = property(lambda self: self._grad_get("_gw_i8"),
@@ -368,20 +373,42 @@ class I8Linear(nn.Module):
         in_f = x_i8.shape[1]
         if parallel.active():
             return self._backward_dp(g_i8, s_g, x_i8, _mask, dev, queued=True)
-        amax = torch.empty(2, dtype=torch.int32, device=dev)
-        dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax[1:2])
-        dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N, amax=amax[0:1])
-        self._gb_sum = _ops.colsum(g_i8)
-        self._gb_s = s_g
+        # The dW branch (GEMM, bias column sums, scale, requant) runs on a side stream forked
+        # here: nothing of the dX chain waits for it, and its memory-bound kernels share the
+        # SMs with the next layer's dX GEMM.  The optimizer (any read of the stashed
+        # gradient) joins it through ``_dw_event``.
+        cur = torch.cuda.current_stream(dev)
+        side = _dw_stream(dev)
+        side.wait_stream(cur)
         key_w = _sr.reserve_key()  # the dW site's key, then the dX site's (the reference's order)
-        s_dx = _scale.from_amax(amax[1:2], s_g, self._sw_mean())
+        with torch.cuda.stream(side):
+            amax_w = torch.empty(1, dtype=torch.int32, device=dev)
+            dw_acc = _ops.gemm_s32(g_i8, 1, x_i8, 1, out, in_f, N, amax=amax_w)
+            gb_sum = _ops.colsum(g_i8)
+            s_gw = _scale.from_amax(amax_w, s_g, self.sx)
+            gw_sumsq = torch.empty(1, dtype=torch.int64, device=dev)
+            gw_i8 = _ops.requant_dev(dw_acc, s_gw, key_w, 0, sumsq=gw_sumsq)
+            done = torch.cuda.Event()
+            done.record(side)
+        g_i8.record_stream(side)  # the main stream may free these while the side stream reads them
+        x_i8.record_stream(side)
+        from .. import graphs
+
+        g = graphs.capturing()
+        if g is not None:
+            g.join(side)
+        amax_x = torch.empty(1, dtype=torch.int32, device=dev)
+        dx_acc = _ops.gemm_s32(g_i8, 0, self.w_i8, 1, N, in_f, out, amax=amax_x)
+        s_dx = _scale.from_amax(amax_x, s_g, self._sw_mean())
         dx_i8 = _ops.requant_dev(dx_acc, s_dx, _sr.new_key(), _sr.row_base(), mask=_mask)
-        s_gw = _scale.from_amax(amax[0:1], s_g, self.sx)
-        self._gw_sumsq = torch.empty(1, dtype=torch.int64, device=dev)
-        self._gw_i8 = _ops.requant_dev(dw_acc, s_gw, key_w, 0, sumsq=self._gw_sumsq)
-        self._gw_sumsq_of = self._gw_i8
+        self._gb_sum = gb_sum
+        self._gb_s = s_g
+        self._gw_sumsq = gw_sumsq
+        self._gw_i8 = gw_i8
+        self._gw_sumsq_of = gw_i8
         self._gw_s = s_gw
         self._gw_rows = None
+        self._dw_event = done
         return dx_i8, s_dx
 
     def _backward_dp(self, g_i8, s_g, x_i8, mask, dev, queued: bool = False):
@@ -465,6 +492,17 @@ class I8Linear(nn.Module):
         self._gw_s = s_gw
         self._gw_rows = rows
         self._gb_sum = p["gb"]
+
+
+_DW_STREAMS: dict = {}
+
+
+def _dw_stream(dev: torch.device) -> torch.cuda.Stream:
+    """The side stream of the single-device queued backward's dW branches (one per device)."""
+    st = _DW_STREAMS.get(dev.index)
+    if st is None:
+        st = _DW_STREAMS[dev.index] = torch.cuda.Stream(dev)
+    return st
 
 
 class I8ReLU(nn.Module):
