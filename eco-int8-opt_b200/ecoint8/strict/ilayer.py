@@ -170,7 +170,10 @@ class I8Linear(nn.Module):
         """Module state for ``torch.save(model)`` (the reference's way to persist): the
         launch caches and in-flight exchange handles are dropped (rebuilt on use); device
         scales of a queued backward are stored as their float values."""
-        self._grad_get("_gw_i8")  # a queued backward's dW branch has finished before the copy
+        ev = self.__dict__.get("_dw_event")
+        if ev is not None:  # a queued backward's dW branch finishes before the tensors are copied
+            self.__dict__["_dw_event"] = None
+            torch.cuda.current_stream(self.w_i8.device).wait_event(ev)
         d = nn.Module.__getstate__(self) if hasattr(nn.Module, "__getstate__") else dict(self.__dict__)
         d = dict(d)
         for k in ("_fwd_cache", "_sw_cache", "_input_gather", "_gather_works", "_sw_mean_cache", "_dw_event"):
