@@ -412,6 +412,82 @@ def eco_step_measurement(device, layers=64, dim=4096, steps=5):
             "lr": 0.05, "momentum": 0.9, "grad_clip": 1.0}
 
 
+def fp32_eco_measurement(device, layers=16, dim=4096, steps=3):
+    """EcoSGDM / EcoAdam (eco.py:50-235): the fused two-launch step over 16 x 4096^2
+    parameters (int8 w, fp32 m and for Adam v, fp32 g; per-row fp32 scales).  Algorithmic
+    bytes per parameter: SGDM reads w, m, g and writes w, m = 1 + 4 + 4 + 1 + 4 = 14; Adam
+    adds v read and written = 22.  The kernels read g twice (the clip's norm pass, then the
+    step): 18 / 26 kernel bytes."""
+    import torch
+
+    from ecoint8 import EcoAdam, EcoSGDM, Int8Linear
+
+    out = {}
+    for name, make, alg in (("sgdm", lambda ls: EcoSGDM(ls, lr=0.05, momentum=0.9), 14),
+                            ("adam", lambda ls: EcoAdam(ls, lr=1e-3), 22)):
+        gen = torch.Generator(device=device).manual_seed(6)
+        lys = []
+        for _ in range(layers):
+            lin = Int8Linear(1, 1, bias=False).to(device)
+            lin.w_i8 = torch.randint(-127, 128, (dim, dim), dtype=torch.int8, device=device, generator=gen)
+            lin.s_w = torch.rand((dim, 1), device=device, generator=gen) * 1e-2 + 1e-3
+            lys.append(lin)
+        grads = [torch.randn((dim, dim), device=device, generator=gen) * 1e-3 for _ in range(layers)]
+        opt = make(lys)
+
+        def step():
+            for lin, g in zip(lys, grads):
+                lin._grad_w = g
+            opt.step()
+
+        t = time_kernel(step, iters=steps, warmup=2)
+        params = layers * dim * dim
+        out[name] = {"params": params, "ms": t * 1e3, "bytes_per_param": alg, "gbs": alg * params / t / 1e9,
+                     "kernel_bytes_per_param": alg + 4}
+        del lys, grads, opt
+        torch.cuda.empty_cache()
+    return out
+
+
+def int8_linear_measurement(device, batch=16384, dim=8192, steps=3):
+    """Int8Linear (layers.py:45-111) forward + backward through autograd at a config-5
+    layer's shape, batch 16384 x 8192 -> 8192: the input's and the output gradient's dynamic
+    quantization on the device and three int8 GEMMs with fp32 dequant epilogues
+    (3 x 2 B dim^2 = 6.6e12 int ops)."""
+    import torch
+
+    from ecoint8.layers import Int8Linear
+
+    gen = torch.Generator(device=device).manual_seed(8)
+    layer = Int8Linear(dim, dim).to(device)
+    x = (torch.randn(batch, dim, device=device, generator=gen) * 2.0).requires_grad_(True)
+    gy = torch.randn(batch, dim, device=device, generator=gen) * 0.05
+
+    def step():
+        y = layer(x)
+        y.backward(gy)
+        x.grad = None
+
+    t = time_kernel(step, iters=steps, warmup=2)
+    ops = 6.0 * batch * dim * dim
+    return {"shape": [batch, dim, dim], "ms": t * 1e3, "tops": ops / t / 1e12}
+
+
+def boundary_measurement(device, rows=16384, classes=1000):
+    """The fused loss boundary (quant.cross_entropy_grad_i8) on config 5's logits: int8
+    [16384, 1000] -> loss, int8 gradient and its device scale (two launches; 1 B read twice
+    and 1 B written per logit)."""
+    import torch
+
+    from ecoint8.quant import cross_entropy_grad_i8
+
+    gen = torch.Generator(device=device).manual_seed(9)
+    logits = torch.randint(-127, 128, (rows, classes), dtype=torch.int8, device=device, generator=gen)
+    labels = torch.randint(0, classes, (rows,), device=device, generator=gen)
+    t = time_kernel(lambda: cross_entropy_grad_i8(logits, 0.05, labels), iters=20, warmup=3)
+    return {"shape": [rows, classes], "ms": t * 1e3, "gbs": 3.0 * rows * classes / t / 1e9}
+
+
 def sgdm_measurement(device, layers=64, dim=4096, steps=3):
     """EcoInt8SGDM's fused step (the replacement of the reference's Triton kernels) over
     64 x 4096^2 parameters: int8 w, m, fp32 g.  Algorithmic bytes 8 per parameter (read
@@ -486,6 +562,73 @@ def reference_layer_steps(max_samples: int, budget_s: float, batch: int = GLOBAL
     return times, info
 
 
+def reference_row_samples(ref) -> dict:
+    """The next rows' reference code on the host cores, one bounded sample each (all host
+    threads): EcoSGDM.step and EcoAdam.step on one Int8Linear(4096, 4096) (eco.py:94-131,
+    182-228), Int8Linear forward + backward at batch 2048 x 8192 -> 8192 (layers.py:45-75,
+    CPU torch._int_mm), and the training loop's loss boundary on config 5's logits
+    [16384, 1000] (examples/i8_demo.py:56-59: cross entropy, its gradient,
+    quantize_tensor_dynamic(g, stochastic=True)).  Seconds per sample and the work it did."""
+    import importlib
+
+    import torch
+
+    eco = importlib.import_module("ecoint8.eco")
+    layers = importlib.import_module("ecoint8.layers")
+    quant = ref["quant"]
+    out = {}
+    torch.manual_seed(0)
+    for name, make in (("eco_sgdm", lambda ls: eco.EcoSGDM(ls, lr=0.05, momentum=0.9)),
+                       ("eco_adam", lambda ls: eco.EcoAdam(ls, lr=1e-3))):
+        lin = layers.Int8Linear(4096, 4096, bias=False)
+        opt = make([lin])
+        g = torch.randn(4096, 4096) * 1e-3
+        lin._grad_w = g.clone()
+        opt.step()  # untimed: state allocation
+        lin._grad_w = g.clone()
+        t0 = time.perf_counter()
+        opt.step()
+        out[name] = {"s": time.perf_counter() - t0, "params": 4096 * 4096}
+    lin = layers.Int8Linear(8192, 8192)
+    x = (torch.randn(2048, 8192) * 2.0).requires_grad_(True)
+    gy = torch.randn(2048, 8192) * 0.05
+    lin(x).backward(gy)  # untimed
+    x.grad = None
+    t0 = time.perf_counter()
+    lin(x).backward(gy)
+    out["int8_linear"] = {"s": time.perf_counter() - t0, "int_ops": 6.0 * 2048 * 8192 * 8192}
+    logits = torch.randint(-127, 128, (16384, 1000), dtype=torch.int8)
+    labels = torch.randint(0, 1000, (16384,))
+    t0 = time.perf_counter()
+    z = (logits.to(torch.float32) * 0.05).requires_grad_(True)
+    loss = torch.nn.functional.cross_entropy(z, labels)
+    (gz,) = torch.autograd.grad(loss, z)
+    quant.quantize_tensor_dynamic(gz, stochastic=True)
+    out["loss_boundary"] = {"s": time.perf_counter() - t0, "logits": 16384 * 1000}
+    return out
+
+
+def row_ratios(out: dict, rows: dict) -> dict:
+    """GPU rate over the reference's host rate for the rows next to the path (work per
+    second each; the work unit of each row is named)."""
+    r = {}
+    try:
+        for k, name in (("sgdm", "eco_sgdm"), ("adam", "eco_adam")):
+            if name in rows:
+                gpu = out["fp32_eco"][k]["params"] / (out["fp32_eco"][k]["ms"] / 1e3)
+                r[name] = {"unit": "parameters/s", "ratio": gpu / (rows[name]["params"] / rows[name]["s"])}
+        if "int8_linear" in rows:
+            r["int8_linear"] = {"unit": "int ops/s", "ratio": out["int8_linear"]["tops"] * 1e12
+                                / (rows["int8_linear"]["int_ops"] / rows["int8_linear"]["s"])}
+        if "loss_boundary" in rows:
+            gpu = out["loss_boundary"]["shape"][0] * out["loss_boundary"]["shape"][1] / (out["loss_boundary"]["ms"] / 1e3)
+            r["loss_boundary"] = {"unit": "logits/s", "ratio": gpu / (rows["loss_boundary"]["logits"]
+                                                                     / rows["loss_boundary"]["s"])}
+    except (KeyError, TypeError, ZeroDivisionError):
+        pass
+    return r
+
+
 def cpu_baseline_subprocess():
     """``cpu_baseline`` of the GPU arm: the reference arm (one untimed and one timed layer
     step of the compiled reference) in a child process, so that the reference's own
@@ -549,6 +692,12 @@ def cpu_baseline_port():
                       f"reference was absent)"}
 
 
+def build_ref_module():
+    from oracle import build_ref
+
+    return build_ref
+
+
 def run_reference_arm(args, rank):
     """``--impl reference``: the reference's own CPU strict step (rank 0 only)."""
     if rank != 0:
@@ -567,6 +716,10 @@ def run_reference_arm(args, rank):
                         f"median {t:.2f} s; x {LAYER_EQUIV:.3f} layer equivalents per training step"}
         ms = 1e3 * t * LAYER_EQUIV
         dtype = "int64"
+        try:  # the rows next to the path, a bounded sample each
+            cb["rows"] = reference_row_samples(build_ref_module().load())
+        except Exception as e:  # noqa: BLE001 -- a missing row does not void the strict step's number
+            cb["rows"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     else:
         cb = cpu_baseline_port()
         value, ms, timed_steps, dtype = cb["value"], 1e3 / cb["value"], None, "int64"
@@ -588,7 +741,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-side", action="store_true", help="skip the GEMM / step / CPU side measurements")
-    ap.add_argument("--only", choices=["gemm", "gemm_sweep", "eco_step", "requant", "sgdm", "peak"],
+    ap.add_argument("--only", choices=["gemm", "gemm_sweep", "eco_step", "requant", "sgdm", "peak", "fp32_eco",
+                                       "int8_linear", "boundary"],
                     help="run one side measurement alone (profiling)")
     ap.add_argument("--eco-layers", type=int, default=64, help="layers of 4096x4096 in the I8ECO step measurement")
     ap.add_argument("--sgdm-layers", type=int, default=64, help="layers of 4096x4096 in the EcoInt8SGDM measurement")
@@ -616,7 +770,8 @@ def main():
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
         res = {"gemm": lambda: gemm_measurements(dev)[0], "gemm_sweep": lambda: gemm_sweep(dev),
-               "requant": lambda: requant_measurement(dev), "sgdm": lambda: sgdm_measurement(dev, layers=args.sgdm_layers),
+               "requant": lambda: requant_measurement(dev), "fp32_eco": lambda: fp32_eco_measurement(dev),
+               "int8_linear": lambda: int8_linear_measurement(dev), "boundary": lambda: boundary_measurement(dev), "sgdm": lambda: sgdm_measurement(dev, layers=args.sgdm_layers),
                "peak": lambda: int8_peak(dev),
                "eco_step": lambda: eco_step_measurement(dev, layers=args.eco_layers)}[args.only]()
         print(json.dumps({args.only: res}))
@@ -827,6 +982,12 @@ def main():
             out["sgdm_step"] = sgdm_measurement(device)
             out["sgdm_step"]["frac_of_hbm"] = out["sgdm_step"]["gbs"] / hbm
             out["requant"] = requant_measurement(device)
+            out["fp32_eco"] = fp32_eco_measurement(device)
+            for k in ("sgdm", "adam"):
+                out["fp32_eco"][k]["frac_of_hbm"] = out["fp32_eco"][k]["gbs"] / hbm
+            out["int8_linear"] = int8_linear_measurement(device)
+            out["int8_linear"]["frac_of_peak"] = out["int8_linear"]["tops"] / peak
+            out["loss_boundary"] = boundary_measurement(device)
             achieved = ops / times["dx"] / 1e12
             out["roofline"] = {"bound": "tensor",
                                "kernel": ("gemm_s8_pair_kernel<0>" if os.environ.get("ECO_GEMM_PAIRS", "1") != "0"
@@ -842,6 +1003,7 @@ def main():
                                "fused_forward": {"achieved": ops / times["fused"] / 1e12,
                                                  "frac": ops / times["fused"] / 1e12 / peak}}
             out["cpu_baseline"] = cpu_baseline_subprocess()
+            out["rows_vs_reference_cpu"] = row_ratios(out, out["cpu_baseline"].get("rows") or {})
         print(json.dumps(out))
     if world > 1:
         parallel.shutdown()
