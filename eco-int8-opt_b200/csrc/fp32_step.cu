@@ -49,6 +49,7 @@ struct Fp32Params {
   eco_fp32_layer_t L[kMaxLayers];
   double* gstats;  // [total_tiles][2]: sum g^2, non-finite count
   double* esum;    // [total_tiles]: sum |e|
+  unsigned char vec[kMaxLayers];  // the layer takes 16-byte loads (cols % 4 == 0, aligned rows)
   // fp32 constants of the reference's expressions (host-rounded like PyTorch's scalars)
   float b_f, omb_f, lr_f, alpha_f, wd_f, eps_f, inv_bc1, inv_bc2, bc1_f, b2_f, omb2_f, adam_eps_f, cinj_f;
 };
@@ -113,6 +114,36 @@ ECO_DEV bool layer_clip(const Fp32Params& P, int l, float& factor, float* norm_o
   return N == 0.0;
 }
 
+// One element of EcoSGDM.step / EcoAdam.step (eco.py:107-128, 196-226) in the reference's
+// PyTorch fp32 operations: returns the new weight (as a float in [-127, 127]), momentum,
+// second moment (Adam) and the error e.
+template <bool ADAM>
+ECO_DEV void step_elem(const Fp32Params& P, float w8, float m, float v_in, float g, float u, float sw, float s,
+                       bool clip, float factor, float& q, float& m_n, float& v_n, float& e) {
+  if (clip) g = __fmul_rn(g, factor);                         // g.mul_(clip / (n + EPS))
+  const float wf = __fmul_rn(w8, sw);                         // layer.w_fp32()
+  if (P.H.weight_decay != 0.0) g = __fmaf_rn(P.wd_f, wf, g);  // g.add_(w_fp32, alpha=wd)
+  float th, m_t, eta = 0.0f;
+  v_n = 0.0f;
+  if (!ADAM) {
+    m_t = __fadd_rn(__fmul_rn(m, P.b_f), __fmul_rn(g, P.omb_f));  // m * b + g * (1 - b)
+    th = __fsub_rn(wf, __fmul_rn(P.lr_f, m_t));                   // w_fp32 - lr * m_tilde
+  } else {
+    m_t = __fmaf_rn(P.omb_f, g, __fmul_rn(m, P.b_f));                        // m.mul_(b1).add_(g, alpha=1-b1)
+    v_n = __fmaf_rn(P.omb2_f, __fmul_rn(g, g), __fmul_rn(v_in, P.b2_f));    // v.mul_(b2).addcmul_(g, g, 1-b2)
+    const float v_hat = __fadd_rn(__fsqrt_rn(__fmul_rn(v_n, P.inv_bc2)), P.adam_eps_f);
+    eta = __fmul_rn(__frcp_rn(__fmul_rn(P.bc1_f, v_hat)), P.lr_f);          // lr / (bc1 * v_hat)
+    th = __fsub_rn(wf, __fmul_rn(eta, __fmul_rn(m_t, P.inv_bc1)));         // w_fp32 - eta * (m / bc1)
+  }
+  const float x = __fdiv_rn(th, __fadd_rn(s, P.eps_f));    // quantize_symmetric: x / (s + EPS)
+  q = fminf(fmaxf(floorf(__fadd_rn(x, u)), -127.0f), 127.0f);
+  e = __fsub_rn(th, __fmul_rn(q, s));                      // th - w_new.float() * s_fixed
+  if (!ADAM)
+    m_n = __fadd_rn(m_t, __fmul_rn(P.alpha_f, e));  // m_tilde + alpha * e
+  else
+    m_n = __fadd_rn(m_t, __fmul_rn(e, __fmul_rn(__frcp_rn(eta), P.cinj_f)));  // m + e * (c / eta)
+}
+
 template <bool ADAM>
 __global__ void __launch_bounds__(kThreads) fp32_step_kernel(const __grid_constant__ Fp32Params P) {
   __shared__ double sh_e[kThreads / 32];
@@ -139,56 +170,71 @@ __global__ void __launch_bounds__(kThreads) fp32_step_kernel(const __grid_consta
     const i64 e0 = (t - P.T.tile_begin[l]) * kTile, e1 = min(n, e0 + kTile);
     const bool philox = P.H.sr_mode == ECO_SR_PHILOX;
     double esum = 0.0;
-    for (i64 q0 = e0 + 4 * (i64)threadIdx.x; q0 < e1; q0 += 4 * kThreads) {
-      const i64 r = q0 / L.cols;
-      const i64 c0 = q0 - r * L.cols;
-      // four consecutive elements; a quad may cross a row end when cols % 4 != 0
-      Philox4 rnd{0u, 0u, 0u, 0u};
-      const bool one_row = c0 + 4 <= L.cols;
-      if (philox && one_row && (c0 & 3) == 0) rnd = sr_quad_k(P.keys, L.stream, (uint32_t)r, (uint32_t)(c0 >> 2));
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const i64 i = q0 + k;
-        if (i >= e1) break;
-        const i64 row = one_row ? r : i / L.cols;
-        const i64 col = i - row * L.cols;
-        float u;
-        if (philox) {
-          const uint32_t f = (one_row && (c0 & 3) == 0) ? quad_word(rnd, k)
-                                                          : sr_field(P.H.seed, L.stream, (uint32_t)row, (uint32_t)col);
-          u = __fmul_rn((float)(f >> 8), 0x1p-24f);
-        } else {
-          u = L.u[i];
-        }
-        float g = L.g[i];
-        if (clip) g = __fmul_rn(g, factor);                           // g.mul_(clip / (n + EPS))
-        const float sw = L.sw[row];
-        const float wf = __fmul_rn((float)L.w[i], sw);               // layer.w_fp32()
-        if (P.H.weight_decay != 0.0) g = __fmaf_rn(P.wd_f, wf, g);   // g.add_(w_fp32, alpha=wd)
-        float th, m_t, v_n = 0.0f, eta = 0.0f;
-        if (!ADAM) {
-          m_t = __fadd_rn(__fmul_rn(L.m[i], P.b_f), __fmul_rn(g, P.omb_f));  // m * b + g * (1 - b)
-          th = __fsub_rn(wf, __fmul_rn(P.lr_f, m_t));                        // w_fp32 - lr * m_tilde
-        } else {
-          m_t = __fmaf_rn(P.omb_f, g, __fmul_rn(L.m[i], P.b_f));  // m.mul_(b1).add_(g, alpha=1-b1)
-          v_n = __fmaf_rn(P.omb2_f, __fmul_rn(g, g), __fmul_rn(L.v[i], P.b2_f));  // v.mul_(b2).addcmul_(g, g, 1-b2)
-          const float v_hat = __fadd_rn(__fsqrt_rn(__fmul_rn(v_n, P.inv_bc2)), P.adam_eps_f);
-          eta = __fmul_rn(__frcp_rn(__fmul_rn(P.bc1_f, v_hat)), P.lr_f);      // lr / (bc1 * v_hat)
-          th = __fsub_rn(wf, __fmul_rn(eta, __fmul_rn(m_t, P.inv_bc1)));     // w_fp32 - eta * (m / bc1)
-        }
-        const float s = L.s_fixed[row];
-        const float v = __fdiv_rn(th, __fadd_rn(s, P.eps_f));                // quantize_symmetric: x / (s + EPS)
-        const float q = fminf(fmaxf(floorf(__fadd_rn(v, u)), -127.0f), 127.0f);
-        const float e = __fsub_rn(th, __fmul_rn(q, s));                      // th - w_new.float() * s_fixed
-        float m_n;
-        if (!ADAM)
-          m_n = __fadd_rn(m_t, __fmul_rn(P.alpha_f, e));  // m_tilde + alpha * e
+    if (P.vec[l]) {
+      // whole quads in one row: one 4-byte load of w, 16-byte loads of m, g (and v, u),
+      // the row's scales once, the same operations per element in the same order
+      const uint32_t cols = (uint32_t)L.cols;
+      for (i64 q0 = e0 + 4 * (i64)threadIdx.x; q0 < e1; q0 += 4 * kThreads) {
+        const uint32_t r = (uint32_t)q0 / cols;
+        const uint32_t c0 = (uint32_t)q0 - r * cols;
+        Philox4 rnd{0u, 0u, 0u, 0u};
+        float4 u4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (philox)
+          rnd = sr_quad_k(P.keys, L.stream, r, c0 >> 2);
         else
-          m_n = __fadd_rn(m_t, __fmul_rn(e, __fmul_rn(__frcp_rn(eta), P.cinj_f)));  // m + e * (c / eta)
-        L.w[i] = (int8_t)q;
-        L.m[i] = m_n;
-        if (ADAM) L.v[i] = v_n;
-        esum += (double)fabsf(e);
+          u4 = *reinterpret_cast<const float4*>(L.u + q0);
+        const uint32_t w4 = *reinterpret_cast<const uint32_t*>(L.w + q0);
+        const float4 m4 = *reinterpret_cast<const float4*>(L.m + q0);
+        const float4 g4 = *reinterpret_cast<const float4*>(L.g + q0);
+        float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ADAM) v4 = *reinterpret_cast<const float4*>(L.v + q0);
+        const float sw = L.sw[r], sf = L.s_fixed[r];
+        const float mi[4] = {m4.x, m4.y, m4.z, m4.w}, gi[4] = {g4.x, g4.y, g4.z, g4.w};
+        const float vi[4] = {v4.x, v4.y, v4.z, v4.w}, ui[4] = {u4.x, u4.y, u4.z, u4.w};
+        int qo[4];
+        float mo[4], vo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float u = philox ? __fmul_rn((float)(quad_word(rnd, k) >> 8), 0x1p-24f) : ui[k];
+          float q, e;
+          step_elem<ADAM>(P, (float)sbyte(w4, k), mi[k], vi[k], gi[k], u, sw, sf, clip, factor, q, mo[k], vo[k], e);
+          qo[k] = (int)q;
+          esum += (double)fabsf(e);
+        }
+        *reinterpret_cast<uint32_t*>(L.w + q0) = pack4(qo[0], qo[1], qo[2], qo[3]);
+        *reinterpret_cast<float4*>(L.m + q0) = make_float4(mo[0], mo[1], mo[2], mo[3]);
+        if (ADAM) *reinterpret_cast<float4*>(L.v + q0) = make_float4(vo[0], vo[1], vo[2], vo[3]);
+      }
+    } else {
+      for (i64 q0 = e0 + 4 * (i64)threadIdx.x; q0 < e1; q0 += 4 * kThreads) {
+        const i64 r = q0 / L.cols;
+        const i64 c0 = q0 - r * L.cols;
+        // four consecutive elements; a quad may cross a row end when cols % 4 != 0
+        Philox4 rnd{0u, 0u, 0u, 0u};
+        const bool one_row = c0 + 4 <= L.cols;
+        if (philox && one_row && (c0 & 3) == 0) rnd = sr_quad_k(P.keys, L.stream, (uint32_t)r, (uint32_t)(c0 >> 2));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const i64 i = q0 + k;
+          if (i >= e1) break;
+          const i64 row = one_row ? r : i / L.cols;
+          const i64 col = i - row * L.cols;
+          float u;
+          if (philox) {
+            const uint32_t f = (one_row && (c0 & 3) == 0) ? quad_word(rnd, k)
+                                                            : sr_field(P.H.seed, L.stream, (uint32_t)row, (uint32_t)col);
+            u = __fmul_rn((float)(f >> 8), 0x1p-24f);
+          } else {
+            u = L.u[i];
+          }
+          float q, m_n, v_n, e;
+          step_elem<ADAM>(P, (float)L.w[i], L.m[i], ADAM ? L.v[i] : 0.0f, L.g[i], u, L.sw[row], L.s_fixed[row], clip,
+                          factor, q, m_n, v_n, e);
+          L.w[i] = (int8_t)q;
+          L.m[i] = m_n;
+          if (ADAM) L.v[i] = v_n;
+          esum += (double)fabsf(e);
+        }
       }
     }
     const double E = block_sum(esum, sh_e);
@@ -228,6 +274,13 @@ extern "C" int eco_fp32_eco_step(const eco_fp32_layer_t* layers, int n_layers, c
   P.T.total_tiles = tiles;
   ECO_REQUIRE(scratch_len >= 3 * tiles, ECO_ERR_ARG, "eco_fp32_eco_step: scratch needs %lld doubles",
               (long long)(3 * tiles));
+  for (int l = 0; l < n_layers; ++l) {  // 16-byte loads need whole quads on aligned rows
+    const eco_fp32_layer_t& L = P.L[l];
+    const bool w_al = (reinterpret_cast<uintptr_t>(L.w) & 3) == 0;
+    P.vec[l] = (unsigned char)(L.cols % 4 == 0 && L.rows * L.cols < (1ll << 32) && w_al &&
+                               eco_aligned16(L.m) && eco_aligned16(L.g) && (hyper->kind == 0 || eco_aligned16(L.v)) &&
+                               (hyper->sr_mode == ECO_SR_PHILOX || eco_aligned16(L.u)));
+  }
   P.gstats = scratch;
   P.esum = scratch + 2 * tiles;
   const eco_fp32_hyper_t& H = *hyper;
