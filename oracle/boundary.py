@@ -100,7 +100,8 @@ def mnist_batch(index: int, batch: int = MNIST_B):
     return X, y
 
 
-MNIST_GOLDEN_STEPS = 469  # steps of the MNIST-shaped run pinned by the golden fixture: one epoch of 60000 at 128
+MNIST_GOLDEN_STEPS = 2345  # steps of the MNIST-shaped run pinned by the golden fixture: 5 epochs of 60000 at 128
+MNIST_EPOCH_STEPS = 469  # one epoch (the CPU oracle test checks this many)
 
 WIDE_D, WIDE_C, WIDE_B = 8192, 1000, 64  # config-5 layer widths, the golden fixture's batch
 

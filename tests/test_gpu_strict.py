@@ -86,7 +86,7 @@ def test_blob_training_replay_matches_reference_every_step(golden):
 
 
 def test_mnist_shaped_replay_matches_reference(golden):
-    """784-256-128-10 at batch 128 (the MNIST-shaped config): one epoch (469 steps), every step bit-exact."""
+    """784-256-128-10 at batch 128 (the MNIST-shaped config): its 5 epochs (2345 steps), every step bit-exact."""
     import ecoint8
     from ecoint8 import I8ECO, I8Linear, I8ReLU, I8Sequential
 
