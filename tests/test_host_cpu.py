@@ -239,3 +239,37 @@ def test_optimizer_and_layers_pickle_like_the_reference():
     assert not hasattr(opt2, "_plan_cache") and opt2._state is None
     assert all(torch.equal(a.w_i8, b.w_i8) for a, b in zip(layers, layers2))
     assert all(torch.equal(a, b) for a, b in zip(opt.m_i8, opt2.m_i8))
+
+
+def test_captured_step_pushes_weight_rows_after_each_replay(monkeypatch):
+    """Under the peer exchange, a step being captured as a CUDA graph does not record its
+    weight-row pushes (the graph would wait for them at every replay's end): it leaves
+    them to a replay hook; an uncaptured step pushes at once."""
+    from ecoint8 import graphs, parallel
+
+    pushed = []
+
+    class FakePeer:
+        def push_weight_rows(self, bufs, lo, hi):
+            pushed.append((bufs, lo, hi))
+
+    class FakeGraph:
+        def __init__(self):
+            self.hooks = []
+
+        def on_replay(self, fn):
+            self.hooks.append(fn)
+
+    bufs = object()
+    monkeypatch.setattr(parallel, "_PEER", FakePeer())
+    monkeypatch.setattr(parallel, "peer_bufs", lambda layer, b=None: bufs)
+    parallel.gather_rows("layer", (8, 16))  # eager: pushed at once
+    assert pushed == [(bufs, 8, 16)]
+    g = FakeGraph()
+    monkeypatch.setattr(graphs, "_ACTIVE", g)
+    parallel.gather_rows("layer", (8, 16))  # captured: nothing recorded, one hook
+    assert pushed == [(bufs, 8, 16)] and len(g.hooks) == 1
+    monkeypatch.setattr(graphs, "_ACTIVE", None)
+    for _ in range(3):  # every replay is followed by the push
+        g.hooks[0]()
+    assert pushed == [(bufs, 8, 16)] * 4
