@@ -6,9 +6,9 @@
 //   q = clamp(round(x / (s + 1e-8)), -127, 127)                     (quant.py:21-28)
 //
 // PyTorch divides a CUDA tensor by a Python scalar as a multiply by the scalar's
-// reciprocal, taken in double and rounded to fp32, and torch.round rounds half to even; both are reproduced here, so q is the
-// reference's bit for bit.  s goes to the device as double bits (scale_out[0]), where the
-// dequantizing GEMM epilogue reads it.
+// reciprocal, taken in double and rounded to fp32, and torch.round rounds half to even;
+// both are reproduced here, so q is the reference's bit for bit.  s goes to the device as
+// double bits (scale_out[0]), where the dequantizing GEMM epilogue reads it.
 #include <algorithm>
 
 #include "abi.cuh"

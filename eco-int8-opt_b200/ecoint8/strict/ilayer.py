@@ -156,9 +156,9 @@ class I8Linear(nn.Module):
 
     # Per-call bookkeeping attributes bypass nn.Module.__setattr__ (none is a
     # parameter, buffer or submodule; properties still apply).
-    _PLAIN_ATTRS = frozenset({"_cache_x", "_dw_pending", "_dw_event", "_fwd_cache", "_gb_s", "_gb_sum", "_gw_rows", "_gw_s",
-                              "_gw_i8", "_gw_sumsq", "_gw_sumsq_of", "_sw_cache", "_input_gather",
-                              "_gather_works"})
+    _PLAIN_ATTRS = frozenset({"_cache_x", "_dw_pending", "_dw_event", "_fwd_cache", "_gb_s", "_gb_sum",
+                              "_gw_rows", "_gw_s", "_gw_i8", "_gw_sumsq", "_gw_sumsq_of", "_sw_cache",
+                              "_input_gather", "_gather_works"})
 
     def __setattr__(self, name, value):
         if name in I8Linear._PLAIN_ATTRS:
