@@ -103,11 +103,11 @@ def mnist_batch(index: int, batch: int = MNIST_B):
 MNIST_GOLDEN_STEPS = 2345  # steps of the MNIST-shaped run pinned by the golden fixture: 5 epochs of 60000 at 128
 MNIST_EPOCH_STEPS = 469  # one epoch (the CPU oracle test checks this many)
 
-WIDE_D, WIDE_C, WIDE_B = 8192, 1000, 64  # config-5 layer widths, the golden fixture's batch
+WIDE_D, WIDE_C, WIDE_B = 8192, 1000, 1024  # config-5 layer widths, the golden fixture's batch
 
 
 def wide_batch():
-    """Config-5-shaped inputs: Gaussian features ``[64, 8192]`` and labels uniform over 1000
+    """Config-5-shaped inputs: Gaussian features ``[1024, 8192]`` and labels uniform over 1000
     classes, from their own generator (seed 2000)."""
     import torch
 

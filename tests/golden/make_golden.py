@@ -214,7 +214,7 @@ def gen_mnist(ref, bnd, nsteps):
 
 
 def gen_wide(ref, bnd, nsteps: int):
-    """Config-5 widths: I8Linear(8192, 8192) + I8ReLU + I8Linear(8192, 1000) at batch 64,
+    """Config-5 widths: I8Linear(8192, 8192) + I8ReLU + I8Linear(8192, 1000) at batch 1024,
     Gaussian inputs quantized with the calibrated entry scale, random labels, I8ECO lr 0.05
     momentum 0.9; digests after every step."""
     import torch
@@ -466,7 +466,7 @@ def main():
         "gemm_requant.json": lambda: gen_gemm_requant(ref),
         "eco_step.json": lambda: gen_eco_step(ref),
         "sgdm_triton.json": lambda: gen_sgdm_triton(ref),
-        "wide_train.json": lambda: gen_wide(ref, bnd, 2),
+        "wide_train.json": lambda: gen_wide(ref, bnd, 3),
         "fp32_eco.json": lambda: gen_fp32_eco(ref),
         "int8_linear.json": lambda: gen_int8_linear(ref),
     }
