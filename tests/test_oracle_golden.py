@@ -181,6 +181,42 @@ def test_mnist_shaped_training_bit_exact(golden):
         assert fhex(opt.stats["mean_abs_e"]) == st["mean_abs_e"], t
 
 
+def test_config5_width_first_step_bit_exact(golden):
+    """Config 5's widths (I8Linear(8192, 8192) + I8ReLU + I8Linear(8192, 1000)) at batch 1024:
+    the oracle reproduces the reference's calibration and first training step (every
+    tensor digest and scale; the GPU test replays all three recorded steps)."""
+    d = golden("wide_train.json")
+    torch.manual_seed(0)
+    net = ost.I8Sequential(ost.I8Linear.seeded(bnd.WIDE_D, bnd.WIDE_D), ost.I8ReLU(),
+                           ost.I8Linear.seeded(bnd.WIDE_D, bnd.WIDE_C))
+    assert [digest(l.w_i8) for l in net.int8_layers()] == d["init"]
+    draws = ost.TorchDraws()
+    X, y = bnd.wide_batch()
+    x0, sx0 = bnd.quantize_tensor_dynamic(X, stochastic=False)
+    cal, _ = net.calibrate(x0.numpy(), sx0, draws)
+    assert digest(cal) == d["calib"]
+    assert [fhex(l.sy) for l in net.int8_layers()] == d["sy"]
+    sx = net.int8_layers()[0].sx
+    x_i8 = torch.clamp(torch.round(X / sx), -127, 127).to(torch.int8).numpy()
+    assert digest(x_i8) == d["x_i8"]
+    opt = ost.I8ECO(net.int8_layers(), lr=0.05, momentum=0.9)
+    st = d["steps"][0]
+    logits, s_out = net.forward_i8(x_i8, draws)
+    assert digest(logits) == st["logits"] and fhex(s_out) == st["s_out"]
+    _, g_fp = bnd.ce_grad(torch.from_numpy(logits), s_out, y)
+    g_i8, s_g = bnd.quantize_tensor_dynamic(g_fp, stochastic=True)
+    assert digest(g_i8.numpy()) == st["g"] and fhex(s_g) == st["s_g"]
+    net.backward_i8(g_i8.numpy(), s_g, draws)
+    for layer, gw in zip(net.int8_layers(), st["grads"]):
+        assert digest(layer._gw_i8) == gw["gw"] and fhex(layer._gw_s) == gw["gw_s"]
+        assert digest(layer._gb_sum) == gw["gb"]
+    opt.step(draws)
+    for i, (layer, ls) in enumerate(zip(net.int8_layers(), st["layers"])):
+        assert digest(layer.w_i8) == ls["w"] and digest(opt.m_i8[i]) == ls["m"], i
+        assert digest(layer.b_acc) == ls["b"] and fhex(opt.s_m[i]) == ls["s_m"], i
+    assert fhex(opt.stats["mean_abs_e"]) == st["mean_abs_e"]
+
+
 def test_standalone_eco_step_golden(golden):
     d = golden("eco_step.json")
     torch.manual_seed(5)
